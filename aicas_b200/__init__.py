@@ -1,0 +1,39 @@
+"""aicas_b200: sm_100a attention backend for the Qwen3-VL-2B inference hot path.
+
+Public surface = the reference package ``triton_qwen3vl``'s ``__all__``
+(triton_qwen3vl/__init__.py:1-16 in the reference project) plus the operators
+it leaves to Hugging Face or lacks: :func:`rope_kv_append`,
+:func:`gqa_decode_partial` and :func:`merge_partials`.
+"""
+from . import _native
+from .backends import TEXT_BACKEND_KEY, VISION_BACKEND_KEY, text_triton_attention, vision_triton_attention
+from .ops import (
+    gqa_decode_attention,
+    gqa_decode_partial,
+    gqa_flash_attention,
+    merge_partials,
+    rope_kv_append,
+    varlen_flash_attention,
+)
+from .patch import install_qwen3vl_triton_attention
+
+# Compatibility name: in the reference it says whether Triton imported
+# (dense_flash_attention.py:7-15); here it says whether the native library loads.
+TRITON_AVAILABLE = _native.available()
+NATIVE_AVAILABLE = TRITON_AVAILABLE
+
+__all__ = [
+    "NATIVE_AVAILABLE",
+    "TEXT_BACKEND_KEY",
+    "TRITON_AVAILABLE",
+    "VISION_BACKEND_KEY",
+    "gqa_decode_attention",
+    "gqa_decode_partial",
+    "gqa_flash_attention",
+    "install_qwen3vl_triton_attention",
+    "merge_partials",
+    "rope_kv_append",
+    "text_triton_attention",
+    "varlen_flash_attention",
+    "vision_triton_attention",
+]

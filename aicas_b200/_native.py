@@ -1,0 +1,173 @@
+"""ctypes binding of ``libaicas_b200.so`` (the C ABI in ``include/aicas_b200.h``).
+
+The structures below mirror the C structs field by field; ``tests`` compile the
+header with gcc and compare ``sizeof``/``offsetof`` against these definitions.
+Loading is lazy and loud: any operator call without the library raises
+``RuntimeError`` naming the build command; nothing falls back to PyTorch.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "lib" / "libaicas_b200.so"
+
+DTYPE_F32 = 0
+DTYPE_F16 = 1
+DTYPE_BF16 = 2
+
+OK = 0
+ERR_INVALID = 1
+ERR_UNSUPPORTED = 2
+ERR_CUDA = 3
+ERR_WORKSPACE = 4
+
+DEVERR_WAIT_TIMEOUT = 1
+DEVERR_TMEM = 2
+
+CAP_DECODE = 1
+CAP_MERGE = 2
+CAP_PREFILL_TCGEN05 = 4
+CAP_VARLEN_TCGEN05 = 8
+CAP_ROPE_APPEND = 16
+
+_i64 = ctypes.c_int64
+_i32 = ctypes.c_int32
+_vp = ctypes.c_void_p
+_f32 = ctypes.c_float
+
+
+class DecodeParams(ctypes.Structure):
+    _fields_ = [
+        ("q", _vp), ("k", _vp), ("v", _vp), ("out", _vp),
+        ("lse", _vp), ("partial_o", _vp), ("kv_lens", _vp),
+        ("q_stride_b", _i64), ("q_stride_h", _i64),
+        ("k_stride_b", _i64), ("k_stride_h", _i64),
+        ("v_stride_b", _i64), ("v_stride_h", _i64),
+        ("o_stride_b", _i64), ("o_stride_h", _i64),
+        ("batch", _i32), ("num_q_heads", _i32), ("num_kv_heads", _i32), ("head_dim", _i32),
+        ("kv_capacity", _i32), ("dtype", _i32), ("sm_scale", _f32), ("split_tokens", _i32),
+    ]
+
+
+class MergeParams(ctypes.Structure):
+    _fields_ = [
+        ("partial_o", _vp), ("partial_lse", _vp), ("out", _vp), ("lse", _vp),
+        ("o_stride_b", _i64), ("o_stride_h", _i64),
+        ("num_partials", _i32), ("batch", _i32), ("num_heads", _i32), ("head_dim", _i32),
+        ("dtype", _i32),
+    ]
+
+
+class FmhaParams(ctypes.Structure):
+    _fields_ = [
+        ("q", _vp), ("k", _vp), ("v", _vp), ("out", _vp),
+        ("q_stride_b", _i64), ("q_stride_h", _i64), ("q_stride_s", _i64),
+        ("k_stride_b", _i64), ("k_stride_h", _i64), ("k_stride_s", _i64),
+        ("v_stride_b", _i64), ("v_stride_h", _i64), ("v_stride_s", _i64),
+        ("o_stride_b", _i64), ("o_stride_h", _i64), ("o_stride_s", _i64),
+        ("batch", _i32), ("num_q_heads", _i32), ("num_kv_heads", _i32), ("seq_len_q", _i32),
+        ("seq_len_kv", _i32), ("head_dim", _i32), ("dtype", _i32), ("sm_scale", _f32),
+        ("cu_seqlens_q", _vp), ("cu_seqlens_k", _vp), ("num_seqs", _i32),
+    ]
+
+
+class RopeAppendParams(ctypes.Structure):
+    _fields_ = [
+        ("q_in", _vp), ("q_out", _vp), ("k_in", _vp), ("v_in", _vp), ("cos", _vp), ("sin", _vp),
+        ("k_cache", _vp), ("v_cache", _vp), ("positions", _vp), ("kv_lens_out", _vp),
+        ("q_norm_weight", _vp), ("k_norm_weight", _vp), ("norm_eps", _f32),
+        ("qi_stride_b", _i64), ("qi_stride_h", _i64), ("qi_stride_s", _i64),
+        ("qo_stride_b", _i64), ("qo_stride_h", _i64), ("qo_stride_s", _i64),
+        ("k_stride_b", _i64), ("k_stride_h", _i64), ("k_stride_s", _i64),
+        ("v_stride_b", _i64), ("v_stride_h", _i64), ("v_stride_s", _i64),
+        ("cs_stride_b", _i64), ("cs_stride_s", _i64),
+        ("kc_stride_b", _i64), ("kc_stride_h", _i64),
+        ("vc_stride_b", _i64), ("vc_stride_h", _i64),
+        ("batch", _i32), ("num_q_heads", _i32), ("num_kv_heads", _i32), ("seq_len", _i32),
+        ("head_dim", _i32), ("capacity", _i32), ("dtype", _i32), ("cs_dtype", _i32),
+    ]
+
+
+# name -> (restype, argtypes); exactly the functions declared in include/aicas_b200.h
+EXPORTS = {
+    "aicas_decode_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(DecodeParams)]),
+    "aicas_decode_gqa": (ctypes.c_int, [ctypes.POINTER(DecodeParams), _vp, ctypes.c_size_t, _vp]),
+    "aicas_merge_partials": (ctypes.c_int, [ctypes.POINTER(MergeParams), _vp]),
+    "aicas_prefill_gqa_causal": (ctypes.c_int, [ctypes.POINTER(FmhaParams), _vp]),
+    "aicas_varlen_attention": (ctypes.c_int, [ctypes.POINTER(FmhaParams), _vp]),
+    "aicas_rope_kv_append": (ctypes.c_int, [ctypes.POINTER(RopeAppendParams), _vp]),
+    "aicas_version": (ctypes.c_char_p, []),
+    "aicas_capabilities": (ctypes.c_uint32, []),
+    "aicas_last_error": (ctypes.c_char_p, []),
+    "aicas_device_error_flags": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int]),
+}
+
+_lib: ctypes.CDLL | None = None
+_load_error: str | None = None
+
+
+def _load() -> ctypes.CDLL:
+    global _lib, _load_error
+    if _lib is not None:
+        return _lib
+    path = Path(os.environ.get("AICAS_B200_LIB", LIB_PATH))
+    if not path.exists():
+        _load_error = (
+            f"native library {path} is missing; build it with `python -m aicas_b200.build` "
+            "(nvcc for sm_100a). The attention operators have no CPU fallback."
+        )
+        raise RuntimeError(_load_error)
+    lib = ctypes.CDLL(str(path))
+    for name, (res, args) in EXPORTS.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def lib() -> ctypes.CDLL:
+    """Returns the loaded library, raising RuntimeError when it is unavailable."""
+    return _load()
+
+
+def available() -> bool:
+    try:
+        _load()
+        return True
+    except (RuntimeError, OSError):
+        return False
+
+
+def library_path() -> Path:
+    return Path(os.environ.get("AICAS_B200_LIB", LIB_PATH))
+
+
+def last_error() -> str:
+    return lib().aicas_last_error().decode(errors="replace")
+
+
+def check(rc: int, what: str) -> None:
+    """Turns a C-ABI status into the reference's exception types."""
+    if rc == OK:
+        return
+    msg = f"{what}: {last_error()}"
+    if rc in (ERR_INVALID, ERR_UNSUPPORTED, ERR_WORKSPACE):
+        raise ValueError(msg)
+    raise RuntimeError(msg)
+
+
+def version() -> str:
+    return lib().aicas_version().decode()
+
+
+def capabilities() -> int:
+    return int(lib().aicas_capabilities())
+
+
+def device_error_flags(clear: bool = False) -> int:
+    flags = ctypes.c_uint32(0)
+    check(lib().aicas_device_error_flags(ctypes.byref(flags), int(clear)), "aicas_device_error_flags")
+    return int(flags.value)

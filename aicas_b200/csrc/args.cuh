@@ -1,0 +1,57 @@
+// Argument blocks passed by value to the kernels (host-filled from the C ABI
+// parameter structs after validation).
+#pragma once
+#include <stdint.h>
+
+namespace aicas {
+
+struct DecodeArgs {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* out;
+  float* lse;
+  float* partial_o;
+  const int32_t* kv_lens;
+  int64_t q_sb, q_sh, k_sb, k_sh, v_sb, v_sh, o_sb, o_sh;
+  int batch, hq, hkv, cap;
+  float scale_log2;
+  int split_tokens;
+  int max_splits;
+  float* ws_o;            // [B*Hkv, max_splits, G, D]
+  float* ws_lse;          // [B*Hkv, max_splits, G]
+  unsigned int* ws_count; // [B*Hkv]
+  unsigned int* err;      // device error word
+};
+
+struct RopeArgs {
+  const void* q_in;
+  void* q_out;
+  const void* k_in;
+  const void* v_in;
+  const void* cos;
+  const void* sin;
+  void* k_cache;
+  void* v_cache;
+  const int32_t* positions;
+  int32_t* kv_lens_out;
+  const void* qw;
+  const void* kw;
+  float eps;
+  int64_t qi_sb, qi_sh, qi_ss, qo_sb, qo_sh, qo_ss;
+  int64_t k_sb, k_sh, k_ss, v_sb, v_sh, v_ss;
+  int64_t cs_sb, cs_ss;
+  int64_t kc_sb, kc_sh, vc_sb, vc_sh;
+  int batch, hq, hkv, seq, hd, cap;
+};
+
+struct MergeArgs {
+  const float* po;
+  const float* plse;
+  void* out;
+  float* lse;
+  int64_t o_sb, o_sh;
+  int np, batch, heads, hd;
+};
+
+}  // namespace aicas

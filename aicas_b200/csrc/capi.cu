@@ -1,0 +1,312 @@
+// C ABI entry points: argument validation, launch planning and error reporting.
+// Nothing here allocates device memory or synchronises the device (except the
+// explicit health query aicas_device_error_flags).
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "common.cuh"
+#include "fmha.cuh"
+
+namespace aicas {
+
+struct DecodeArgs;
+cudaError_t launch_decode(int dtype, int head_dim, int group, const DecodeArgs& a, cudaStream_t st);
+int decode_tile_for(int dtype, int head_dim);
+struct RopeArgs;
+cudaError_t launch_rope_append(int dtype, int cs_dtype, const RopeArgs& a, cudaStream_t st);
+struct MergeArgs;
+cudaError_t launch_merge(int dtype, const MergeArgs& a, cudaStream_t st);
+
+}  // namespace aicas
+
+// The full definitions are needed to fill the argument blocks.
+#include "args.cuh"
+
+namespace {
+
+// The device error word (AICAS_DEVERR_* bits), one per device context.
+__device__ unsigned int g_device_error = 0;
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(AICAS_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+int elem_bytes(int dtype) {
+  switch (dtype) {
+    case AICAS_DTYPE_F32: return 4;
+    case AICAS_DTYPE_F16: return 2;
+    case AICAS_DTYPE_BF16: return 2;
+  }
+  return 0;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+bool stride_ok(int64_t stride, int eb) { return ((stride * eb) & 15) == 0; }
+bool is_pow2_group(int g) { return g == 1 || g == 2 || g == 4 || g == 8; }
+bool head_dim_ok(int d) { return d == 16 || d == 32 || d == 64 || d == 128; }
+
+int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
+// Device address of g_device_error for the current device (cached per device).
+unsigned int* device_error_word() {
+  static unsigned int* cached[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (cached[dev] == nullptr) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_device_error) != cudaSuccess) return nullptr;
+    cached[dev] = static_cast<unsigned int*>(ptr);
+  }
+  return cached[dev];
+}
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// Split-KV plan shared by aicas_decode_workspace_bytes and aicas_decode_gqa.
+struct DecodePlan {
+  int split_tokens;
+  int max_splits;
+  size_t ws_o_off, ws_lse_off, ws_count_off, ws_bytes;
+};
+
+int plan_decode(const aicas_decode_params* p, DecodePlan* out) {
+  const int tile = aicas::decode_tile_for(p->dtype, p->head_dim);
+  int split = p->split_tokens;
+  if (split < 0 || (split > 0 && split % tile != 0))
+    return fail(AICAS_ERR_UNSUPPORTED, "split_tokens=%d must be 0 or a positive multiple of %d",
+                p->split_tokens, tile);
+  if (split == 0) {
+    // enough work units for ~8 resident waves of 2 CTAs per SM, in whole tiles
+    const int64_t total = (int64_t)p->batch * p->num_kv_heads * (int64_t)(p->kv_capacity > 0 ? p->kv_capacity : 1);
+    const int64_t target = (int64_t)sm_count() * 2 * 8;
+    int64_t s = (total + target - 1) / target;
+    s = (s + tile - 1) / tile * tile;
+    if (s < 4 * tile) s = 4 * tile;
+    if (s > 16384) s = 16384;
+    split = (int)s;
+  }
+  const int cap = p->kv_capacity > 0 ? p->kv_capacity : 1;
+  out->split_tokens = split;
+  out->max_splits = (cap + split - 1) / split;
+  const int g = p->num_q_heads / p->num_kv_heads;
+  const size_t units = (size_t)p->batch * p->num_kv_heads;
+  size_t off = 0;
+  out->ws_o_off = off;
+  off = align_up(off + units * out->max_splits * g * p->head_dim * sizeof(float), 256);
+  out->ws_lse_off = off;
+  off = align_up(off + units * out->max_splits * g * sizeof(float), 256);
+  out->ws_count_off = off;
+  off = align_up(off + units * sizeof(unsigned int), 256);
+  out->ws_bytes = out->max_splits > 1 ? off : 0;
+  return AICAS_OK;
+}
+
+int check_decode(const aicas_decode_params* p) {
+  if (p == nullptr) return fail(AICAS_ERR_INVALID, "params is NULL");
+  if (p->q == nullptr || p->k == nullptr || p->v == nullptr)
+    return fail(AICAS_ERR_INVALID, "q, k and v must be non-NULL");
+  if (p->out == nullptr && p->partial_o == nullptr)
+    return fail(AICAS_ERR_INVALID, "one of out / partial_o must be set");
+  if (p->partial_o != nullptr && p->lse == nullptr)
+    return fail(AICAS_ERR_INVALID, "partial_o requires lse");
+  const int eb = elem_bytes(p->dtype);
+  if (eb == 0) return fail(AICAS_ERR_UNSUPPORTED, "unknown dtype %d", p->dtype);
+  if (p->batch < 1 || p->batch > 65535 || p->num_kv_heads < 1 || p->num_kv_heads > 65535 || p->num_q_heads < 1 ||
+      p->kv_capacity < 0)
+    return fail(AICAS_ERR_INVALID, "batch=%d num_q_heads=%d num_kv_heads=%d kv_capacity=%d", p->batch,
+                p->num_q_heads, p->num_kv_heads, p->kv_capacity);
+  if (p->num_q_heads % p->num_kv_heads != 0)
+    return fail(AICAS_ERR_INVALID, "num_q_heads=%d is not a multiple of num_kv_heads=%d", p->num_q_heads,
+                p->num_kv_heads);
+  const int g = p->num_q_heads / p->num_kv_heads;
+  if (!is_pow2_group(g)) return fail(AICAS_ERR_UNSUPPORTED, "GQA group size %d not in {1,2,4,8}", g);
+  if (!head_dim_ok(p->head_dim)) return fail(AICAS_ERR_UNSUPPORTED, "head_dim %d not in {16,32,64,128}", p->head_dim);
+  if (!aligned16(p->q) || !aligned16(p->k) || !aligned16(p->v) || !aligned16(p->out) || !aligned16(p->partial_o))
+    return fail(AICAS_ERR_INVALID, "device pointers must be 16-byte aligned");
+  if (!stride_ok(p->q_stride_b, eb) || !stride_ok(p->q_stride_h, eb) || !stride_ok(p->k_stride_b, eb) ||
+      !stride_ok(p->k_stride_h, eb) || !stride_ok(p->v_stride_b, eb) || !stride_ok(p->v_stride_h, eb))
+    return fail(AICAS_ERR_INVALID, "q/k/v strides must be multiples of 16 bytes");
+  if (p->out != nullptr && (p->o_stride_b < 0 || p->o_stride_h < 0))
+    return fail(AICAS_ERR_INVALID, "negative output stride");
+  if (!(p->sm_scale == p->sm_scale) || p->sm_scale == INFINITY || p->sm_scale == -INFINITY)
+    return fail(AICAS_ERR_INVALID, "sm_scale must be finite");
+  return AICAS_OK;
+}
+
+int check_fmha(const aicas_fmha_params* p, bool varlen) {
+  if (p == nullptr) return fail(AICAS_ERR_INVALID, "params is NULL");
+  if (p->q == nullptr || p->k == nullptr || p->v == nullptr || p->out == nullptr)
+    return fail(AICAS_ERR_INVALID, "q, k, v and out must be non-NULL");
+  if (p->dtype != AICAS_DTYPE_BF16 && p->dtype != AICAS_DTYPE_F16)
+    return fail(AICAS_ERR_UNSUPPORTED, "tensor-core attention needs fp16 or bf16 (dtype %d)", p->dtype);
+  if (p->head_dim != 64 && p->head_dim != 128)
+    return fail(AICAS_ERR_UNSUPPORTED, "tensor-core attention supports head_dim 64 and 128 (got %d)", p->head_dim);
+  if (p->batch < 1 || p->num_q_heads < 1 || p->num_kv_heads < 1 || p->seq_len_q < 0 || p->seq_len_kv < 0)
+    return fail(AICAS_ERR_INVALID, "bad sizes");
+  if (p->num_q_heads % p->num_kv_heads != 0)
+    return fail(AICAS_ERR_INVALID, "num_q_heads %% num_kv_heads != 0");
+  const int eb = 2;
+  if (!aligned16(p->q) || !aligned16(p->k) || !aligned16(p->v) || !aligned16(p->out))
+    return fail(AICAS_ERR_INVALID, "device pointers must be 16-byte aligned");
+  const int64_t st[] = {p->q_stride_b, p->q_stride_h, p->q_stride_s, p->k_stride_b, p->k_stride_h, p->k_stride_s,
+                        p->v_stride_b, p->v_stride_h, p->v_stride_s, p->o_stride_b, p->o_stride_h, p->o_stride_s};
+  for (int64_t s : st)
+    if (s < 0 || !stride_ok(s, eb)) return fail(AICAS_ERR_INVALID, "strides must be non-negative multiples of 16 bytes");
+  if (!(p->sm_scale == p->sm_scale)) return fail(AICAS_ERR_INVALID, "sm_scale is NaN");
+  if (varlen) {
+    if (p->batch != 1) return fail(AICAS_ERR_UNSUPPORTED, "varlen attention needs batch == 1");
+    if (p->num_q_heads != p->num_kv_heads) return fail(AICAS_ERR_UNSUPPORTED, "varlen attention needs Hq == Hkv");
+    if (p->cu_seqlens_q == nullptr || p->cu_seqlens_k == nullptr || p->num_seqs < 0)
+      return fail(AICAS_ERR_INVALID, "cu_seqlens_q/k must be set");
+  } else {
+    if (p->seq_len_q != p->seq_len_kv)
+      return fail(AICAS_ERR_UNSUPPORTED, "causal prefill needs q_len == kv_len (%d vs %d)", p->seq_len_q, p->seq_len_kv);
+  }
+  return AICAS_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* aicas_version(void) { return "aicas_b200 0.1.0 sm_100a abi 1"; }
+
+uint32_t aicas_capabilities(void) {
+  return AICAS_CAP_DECODE | AICAS_CAP_MERGE | AICAS_CAP_ROPE_APPEND | aicas::fmha_capabilities();
+}
+
+const char* aicas_last_error(void) { return g_err; }
+
+int aicas_device_error_flags(uint32_t* flags, int clear) {
+  if (flags == nullptr) return fail(AICAS_ERR_INVALID, "flags is NULL");
+  unsigned int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_device_error, sizeof(v));
+  if (e != cudaSuccess) return cuda_fail(e, "reading the device error word");
+  *flags = v;
+  if (clear) {
+    const unsigned int z = 0;
+    e = cudaMemcpyToSymbol(g_device_error, &z, sizeof(z));
+    if (e != cudaSuccess) return cuda_fail(e, "clearing the device error word");
+  }
+  return AICAS_OK;
+}
+
+size_t aicas_decode_workspace_bytes(const aicas_decode_params* p) {
+  if (check_decode(p) != AICAS_OK) return 0;
+  DecodePlan plan;
+  if (plan_decode(p, &plan) != AICAS_OK) return 0;
+  return plan.ws_bytes;
+}
+
+int aicas_decode_gqa(const aicas_decode_params* p, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_decode(p);
+  if (rc != AICAS_OK) return rc;
+  DecodePlan plan;
+  rc = plan_decode(p, &plan);
+  if (rc != AICAS_OK) return rc;
+  if (plan.ws_bytes > 0 && (workspace == nullptr || workspace_bytes < plan.ws_bytes))
+    return fail(AICAS_ERR_WORKSPACE, "decode needs %zu bytes of zero-initialised workspace (got %zu)", plan.ws_bytes,
+                workspace_bytes);
+  if (workspace != nullptr && (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return fail(AICAS_ERR_INVALID, "workspace must be 256-byte aligned");
+  aicas::DecodeArgs a;
+  a.q = p->q; a.k = p->k; a.v = p->v; a.out = p->out; a.lse = p->lse; a.partial_o = p->partial_o;
+  a.kv_lens = p->kv_lens;
+  a.q_sb = p->q_stride_b; a.q_sh = p->q_stride_h;
+  a.k_sb = p->k_stride_b; a.k_sh = p->k_stride_h;
+  a.v_sb = p->v_stride_b; a.v_sh = p->v_stride_h;
+  a.o_sb = p->o_stride_b; a.o_sh = p->o_stride_h;
+  a.batch = p->batch; a.hq = p->num_q_heads; a.hkv = p->num_kv_heads; a.cap = p->kv_capacity;
+  a.scale_log2 = p->sm_scale * 1.4426950408889634f;
+  a.split_tokens = plan.split_tokens;
+  a.max_splits = plan.max_splits;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  a.ws_o = plan.ws_bytes ? reinterpret_cast<float*>(ws + plan.ws_o_off) : nullptr;
+  a.ws_lse = plan.ws_bytes ? reinterpret_cast<float*>(ws + plan.ws_lse_off) : nullptr;
+  a.ws_count = plan.ws_bytes ? reinterpret_cast<unsigned int*>(ws + plan.ws_count_off) : nullptr;
+  a.err = device_error_word();
+  cudaError_t e = aicas::launch_decode(p->dtype, p->head_dim, p->num_q_heads / p->num_kv_heads, a,
+                                       static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "decode launch");
+  return AICAS_OK;
+}
+
+int aicas_merge_partials(const aicas_merge_params* p, void* stream) {
+  if (p == nullptr) return fail(AICAS_ERR_INVALID, "params is NULL");
+  if (p->partial_o == nullptr || p->partial_lse == nullptr || p->out == nullptr)
+    return fail(AICAS_ERR_INVALID, "partial_o, partial_lse and out must be non-NULL");
+  if (elem_bytes(p->dtype) == 0) return fail(AICAS_ERR_UNSUPPORTED, "unknown dtype %d", p->dtype);
+  if (p->num_partials < 1 || p->batch < 1 || p->num_heads < 1 || p->head_dim < 1 || p->head_dim > 1024)
+    return fail(AICAS_ERR_INVALID, "bad sizes");
+  aicas::MergeArgs a;
+  a.po = p->partial_o; a.plse = p->partial_lse; a.out = p->out; a.lse = p->lse;
+  a.o_sb = p->o_stride_b; a.o_sh = p->o_stride_h;
+  a.np = p->num_partials; a.batch = p->batch; a.heads = p->num_heads; a.hd = p->head_dim;
+  cudaError_t e = aicas::launch_merge(p->dtype, a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "merge launch");
+  return AICAS_OK;
+}
+
+int aicas_rope_kv_append(const aicas_rope_append_params* p, void* stream) {
+  if (p == nullptr) return fail(AICAS_ERR_INVALID, "params is NULL");
+  if (p->q_in == nullptr || p->q_out == nullptr || p->k_in == nullptr || p->v_in == nullptr || p->cos == nullptr ||
+      p->sin == nullptr || p->k_cache == nullptr || p->v_cache == nullptr || p->positions == nullptr)
+    return fail(AICAS_ERR_INVALID, "q_in, q_out, k_in, v_in, cos, sin, k_cache, v_cache and positions must be set");
+  if (elem_bytes(p->dtype) == 0) return fail(AICAS_ERR_UNSUPPORTED, "unknown dtype %d", p->dtype);
+  if (p->cs_dtype != p->dtype && p->cs_dtype != AICAS_DTYPE_F32)
+    return fail(AICAS_ERR_UNSUPPORTED, "cos/sin dtype must equal the tensor dtype or be fp32");
+  if (p->head_dim < 2 || p->head_dim > 128 || (p->head_dim & 1))
+    return fail(AICAS_ERR_UNSUPPORTED, "head_dim must be even and <= 128 (got %d)", p->head_dim);
+  if (p->batch < 1 || p->num_q_heads < 1 || p->num_kv_heads < 1 || p->seq_len < 1 || p->capacity < 0)
+    return fail(AICAS_ERR_INVALID, "bad sizes");
+  aicas::RopeArgs a;
+  a.q_in = p->q_in; a.q_out = p->q_out; a.k_in = p->k_in; a.v_in = p->v_in; a.cos = p->cos; a.sin = p->sin;
+  a.k_cache = p->k_cache; a.v_cache = p->v_cache; a.positions = p->positions; a.kv_lens_out = p->kv_lens_out;
+  a.qw = p->q_norm_weight; a.kw = p->k_norm_weight; a.eps = p->norm_eps;
+  a.qi_sb = p->qi_stride_b; a.qi_sh = p->qi_stride_h; a.qi_ss = p->qi_stride_s;
+  a.qo_sb = p->qo_stride_b; a.qo_sh = p->qo_stride_h; a.qo_ss = p->qo_stride_s;
+  a.k_sb = p->k_stride_b; a.k_sh = p->k_stride_h; a.k_ss = p->k_stride_s;
+  a.v_sb = p->v_stride_b; a.v_sh = p->v_stride_h; a.v_ss = p->v_stride_s;
+  a.cs_sb = p->cs_stride_b; a.cs_ss = p->cs_stride_s;
+  a.kc_sb = p->kc_stride_b; a.kc_sh = p->kc_stride_h; a.vc_sb = p->vc_stride_b; a.vc_sh = p->vc_stride_h;
+  a.batch = p->batch; a.hq = p->num_q_heads; a.hkv = p->num_kv_heads; a.seq = p->seq_len; a.hd = p->head_dim;
+  a.cap = p->capacity;
+  cudaError_t e = aicas::launch_rope_append(p->dtype, p->cs_dtype, a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "rope/append launch");
+  return AICAS_OK;
+}
+
+int aicas_prefill_gqa_causal(const aicas_fmha_params* p, void* stream) {
+  int rc = check_fmha(p, false);
+  if (rc != AICAS_OK) return rc;
+  return aicas::run_fmha(p, /*varlen=*/false, static_cast<cudaStream_t>(stream), device_error_word(), g_err, sizeof(g_err));
+}
+
+int aicas_varlen_attention(const aicas_fmha_params* p, void* stream) {
+  int rc = check_fmha(p, true);
+  if (rc != AICAS_OK) return rc;
+  return aicas::run_fmha(p, /*varlen=*/true, static_cast<cudaStream_t>(stream), device_error_word(), g_err, sizeof(g_err));
+}
+
+}  // extern "C"

@@ -1,0 +1,555 @@
+#!/usr/bin/env python
+"""Benchmark of the Qwen3-VL-2B attention hot path on B200.
+
+Headline (one JSON line on rank 0): config 2 of the baseline — one batched
+decode STEP of the text decoder: for each of 28 layers, the new token's q/k
+are rotated and k/v appended to that layer's padded cache (fused RoPE + append
+kernel), then GQA decode attention runs over each request's valid prefix
+(split-KV decode kernel).  B=64 requests per GPU, 16 q heads / 8 KV heads,
+head_dim 128, bf16, per-request lengths ~ U[256, 4096] in caches padded to 4096.
+The metric is algorithmic HBM bytes moved per second (GB/s), whole job.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 is launched with torchrun, one rank per GPU: every rank runs its own
+batch of 64 requests (decode shards by request, no collective; weak scaling).
+Secondary numbers in the same line: config 5 (B=4, L=131072) sequence-sharded
+across the N ranks with one NCCL all-gather of the (out, LSE) partials, and the
+tensor-core prefill (config 4) / ViT varlen (config 3) kernels when built.
+
+``--impl reference`` times the reference's own CPU path (restated in
+oracle/reference_cpu.py, as the reference is Python and does not travel) on
+the host cores for the same workload and metric.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+METRIC = "decode-attn HBM GB/s (% peak); prefill/ViT attn TFLOPS; scaling 1/2/4/8 GPU"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+B, L_CAP, LAYERS = 64, 4096, 28
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+# ------------------------------------------------------------------ peaks / traffic
+
+
+def load_peaks() -> tuple[dict, str]:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            return {k: float(d[k]) for k in ("hbm_gbs", "bf16_tflops", "bf16_tflops_sustained")}, "measured"
+        except Exception:  # noqa: BLE001
+            pass
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def profiled_traffic(name: str) -> float | None:
+    """dram bytes per launch from a committed ncu summary (a line 'dram_bytes_per_launch: N')."""
+    p = REPO / "profiles" / name
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.strip().startswith("dram_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+# ------------------------------------------------------------------ clocks
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML while running."""
+
+    REASONS = {
+        0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+        0x80: "hw_power_brake_slowdown", 0x2: "applications_clocks_setting", 0x10: "sync_boost",
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.02):
+        self.samples: list[int] = []
+        self.reasons = 0
+        self.max_mhz = None
+        self.err = None
+        self._stop = threading.Event()
+        self._period = period_s
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            phys = int(vis.split(",")[device_index]) if vis else device_index
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(phys)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # noqa: BLE001
+            self._nvml = None
+            self.err = str(e)
+        self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self._nvml.nvmlDeviceGetClockInfo(self._h, self._nvml.NVML_CLOCK_SM))
+                self.reasons |= int(self._nvml.nvmlDeviceGetCurrentClocksEventReasons(self._h))
+            except Exception as e:  # noqa: BLE001
+                self.err = str(e)
+                return
+            time.sleep(self._period)
+
+    def __enter__(self):
+        if self._nvml is not None:
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._t.is_alive():
+            self._t.join()
+
+    def summary(self) -> dict:
+        out = {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+               "reasons": [n for bit, n in self.REASONS.items() if self.reasons & bit], "samples": len(self.samples),
+               "source": "nvml"}
+        if self.err:
+            out["error"] = self.err
+        return out
+
+
+# ------------------------------------------------------------------ distributed helpers
+
+
+def dist_info():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def max_over_ranks(x: float, world: int, device) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int, device):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier(device_ids=[device.index])
+    torch.cuda.synchronize(device)
+
+
+# ------------------------------------------------------------------ workload
+
+
+def step_bytes(lengths: torch.Tensor) -> dict:
+    """Algorithmic bytes of one config-2 step (padded slots are not counted)."""
+    hq, hkv, d, e = 16, 8, 128, 2
+    kv = int(sum(2 * hkv * d * e * (int(n) + 1) for n in lengths))  # K and V of the valid prefix incl. the new token
+    qo = 2 * B * hq * d * e                                         # decode reads q, writes o
+    rope = B * (hq + 2 * hkv) * d * e + 2 * B * d * e + B * hq * d * e + 2 * B * hkv * d * e
+    return {"decode_per_layer": kv + qo, "rope_per_layer": rope, "step": LAYERS * (kv + qo + rope)}
+
+
+class DecodeWorkload:
+    def __init__(self, device, seed: int):
+        import aicas_b200 as ab
+        from aicas_b200 import workloads as wl
+
+        self.ab, self.wl = ab, wl
+        self.device = device
+        self.lengths = wl.cfg2_lengths(0)
+        self.caches = [wl.cfg2_cache(B, L_CAP, layer, seed=seed, device=device) for layer in range(LAYERS)]
+        self.inputs = [wl.cfg2_step_inputs(self.lengths, layer, seed=seed, device=device) for layer in range(LAYERS)]
+        self.lens_after = torch.empty(B, dtype=torch.int32, device=device)
+        self.q_rot = [torch.empty(B, 1, 16, 128, dtype=torch.bfloat16, device=device).transpose(1, 2)
+                      for _ in range(LAYERS)]
+        self.bytes = step_bytes(self.lengths)
+
+    def step(self, decode_events=None):
+        ab, wl = self.ab, self.wl
+        outs = []
+        for layer in range(LAYERS):
+            x = self.inputs[layer]
+            kc, vc = self.caches[layer]
+            ab.rope_kv_append(x.q, x.k, x.v, x.cos, x.sin, kc, vc, x.positions, q_out=self.q_rot[layer],
+                              kv_lens_out=self.lens_after)
+            if decode_events is not None:
+                decode_events[layer][0].record()
+            outs.append(ab.gqa_decode_attention(self.q_rot[layer], kc, vc, sm_scale=wl.SCALE_TEXT,
+                                                num_key_value_groups=2, kv_lens=self.lens_after))
+            if decode_events is not None:
+                decode_events[layer][1].record()
+        return outs
+
+
+def run_ours(args, world, rank, device, peaks, peak_src) -> dict | None:
+    import aicas_b200 as ab
+    from aicas_b200 import _native
+    from aicas_b200 import workloads as wl
+
+    _native.lib()  # loud failure if the library is missing
+    wk = DecodeWorkload(device, seed=rank)
+    torch.cuda.synchronize(device)
+
+    # --- capture the 28-layer step (56 launches) in a CUDA graph, with timing
+    # events around every decode launch recorded as graph nodes
+    cap_stream = torch.cuda.Stream(device)
+    cap_stream.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(cap_stream):
+        for _ in range(max(args.warmup, 3)):
+            wk.step()
+    torch.cuda.current_stream(device).wait_stream(cap_stream)
+    torch.cuda.synchronize(device)
+    def capture(with_events: bool):
+        ev = ([[torch.cuda.Event(enable_timing=True, external=True) for _ in range(2)] for _ in range(LAYERS)]
+              if with_events else None)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=cap_stream):
+            wk.step(decode_events=ev)
+        return g, ev
+
+    try:
+        graph, ev = capture(True)
+        timing_mode = "events recorded as graph nodes around every decode launch of the timed replays"
+    except Exception as exc:  # noqa: BLE001  (older drivers: no timing events in graphs)
+        log(f"event capture failed ({exc}); timing decode launches eagerly")
+        torch.cuda.synchronize(device)
+        graph, ev = capture(False)
+        timing_mode = "eager step with events around each decode launch, after the timed replays"
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
+    torch.cuda.synchronize(device)
+
+    # --- timed region: K graph replays (inputs 571 MB of KV per layer > L2)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world, device)
+    with ClockSampler(device.index) as clocks:
+        start.record()
+        for _ in range(args.steps):
+            graph.replay()
+        end.record()
+        torch.cuda.synchronize(device)
+    elapsed_ms = start.elapsed_time(end)
+    barrier(world, device)
+    elapsed_ms = max_over_ranks(elapsed_ms, world, device)
+    ms_step = elapsed_ms / args.steps
+    value = world * wk.bytes["step"] / (ms_step * 1e-3) / 1e9
+    if ev is not None:
+        # the events hold the launches of the last timed replay (28 decode launches)
+        dec_ms = [a.elapsed_time(b) for a, b in ev]
+    else:
+        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(LAYERS)]
+        wk.step(decode_events=ev)
+        torch.cuda.synchronize(device)
+        dec_ms = [a.elapsed_time(b) for a, b in ev]
+    dec_avg_ms = statistics.mean(dec_ms)
+    achieved = wk.bytes["decode_per_layer"] / (dec_avg_ms * 1e-3) / 1e9
+    roofline = {"bound": "hbm", "kernel": "decode_gqa_kernel<bf16,128,2>", "achieved": round(achieved, 1),
+                "timing": timing_mode, "launches_timed": len(dec_ms),
+                "peak": peaks["hbm_gbs"], "peak_source": f"{peak_src} hbm_gbs", "unit": "GB/s",
+                "frac": round(achieved / peaks["hbm_gbs"], 4),
+                "traffic": profiled_traffic("decode_gqa_cfg2.txt"),
+                "algorithmic_bytes_per_launch": wk.bytes["decode_per_layer"],
+                "avg_launch_us": round(dec_avg_ms * 1e3, 2),
+                "decode_share_of_step": round(dec_avg_ms * LAYERS / ms_step, 3)}
+    del graph
+
+    # --- end to end through the public API with host buffers (eager, no graph)
+    e2e = run_e2e(wk, args, world, device)
+
+    # --- secondary: config 5 split-KV across the ranks
+    split = run_split_kv(args, world, rank, device)
+    fmha = run_fmha_secondary(args, world, device, peaks) if args.secondary else {}
+    line = None
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "cfg2: batched GQA decode step (RoPE + KV append + split-KV decode) x 28 layers",
+                       "batch_per_gpu": B, "layers": LAYERS, "q_heads": 16, "kv_heads": 8, "head_dim": 128,
+                       "kv_capacity": L_CAP, "lengths": "U[256,4096] seed 0", "mean_len": float(wk.lengths.float().mean()),
+                       "parallelism": f"dp{world} (requests sharded, no collective)",
+                       "l2": "inputs larger than L2 (571 MB of valid KV per layer, 30 GB resident)",
+                       "graph": "28-layer step captured in one CUDA graph (56 launches)"},
+            "roofline": roofline,
+            "e2e": e2e,
+            "gpu_launches": args.steps * LAYERS * 2,
+            "clocks": clocks.summary(),
+            "split_kv_cfg5": split,
+            **fmha,
+        }
+    return line
+
+
+def run_e2e(wk: DecodeWorkload, args, world, device) -> dict:
+    """Same step through the public HF-facing API, inputs copied from pinned host
+    memory every step and the attention outputs read back."""
+    from aicas_b200 import backends
+    import aicas_b200 as ab
+
+    class Attn(torch.nn.Module):
+        num_key_value_groups, scaling, is_causal = 2, wk.wl.SCALE_TEXT, True
+
+    mod = Attn()
+    host_in = []
+    for x in wk.inputs:
+        host_in.append([t.cpu().pin_memory() for t in (x.q, x.k, x.v, x.cos, x.sin, x.positions)])
+    host_out = [torch.empty(B, 1, 16, 128, dtype=torch.bfloat16).pin_memory() for _ in range(LAYERS)]
+    h2d = sum(t.numel() * t.element_size() for ts in host_in for t in ts)
+    d2h = sum(t.numel() * t.element_size() for t in host_out)
+    lens_after = torch.empty(B, dtype=torch.int32, device=device)
+
+    def one_step():
+        for layer in range(LAYERS):
+            q, k, v, cos, sin, pos = (t.to(device, non_blocking=True) for t in host_in[layer])
+            kc, vc = wk.caches[layer]
+            q_rot = ab.rope_kv_append(q, k, v, cos, sin, kc, vc, pos, kv_lens_out=lens_after)
+            out, _ = backends.text_triton_attention(mod, q_rot, kc, vc, None, kv_lens=lens_after)
+            host_out[layer].copy_(out, non_blocking=True)
+
+    steps = max(3, min(args.steps, 50))
+    for _ in range(max(args.warmup, 3)):
+        one_step()
+    torch.cuda.synchronize(device)
+    barrier(world, device)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        one_step()
+    torch.cuda.synchronize(device)
+    ms = (time.perf_counter() - t0) * 1e3 / steps
+    ms = max_over_ranks(ms, world, device)
+    return {"value": round(world * wk.bytes["step"] / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+            "ms_per_step": round(ms, 4), "steps": steps, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "api": "aicas_b200.rope_kv_append + backends.text_triton_attention (HF attention interface)",
+            "timing": "wall clock around the step loop, device synchronised"}
+
+
+def run_split_kv(args, world, rank, device) -> dict:
+    """Config 5: B=4, L=131072 sequence-sharded over the ranks (strong scaling)."""
+    import aicas_b200 as ab
+    from aicas_b200 import distributed as adist
+    from aicas_b200 import workloads as wl
+
+    Bq, L = 4, 131072
+    s0, s1 = adist.shard_bounds(L, world, rank)
+    g = wl.generator(5, device)
+    q = wl.randn((Bq, 16, 1, 128), g, torch.bfloat16, device)
+    k = wl.randn((Bq, 8, s1 - s0, 128), g, torch.bfloat16, device)
+    v = wl.randn((Bq, 8, s1 - s0, 128), g, torch.bfloat16, device)
+
+    def once():
+        if world == 1:
+            return ab.gqa_decode_attention(q, k, v, sm_scale=wl.SCALE_TEXT, num_key_value_groups=2)
+        return adist.sharded_gqa_decode(q, k, v, sm_scale=wl.SCALE_TEXT, num_key_value_groups=2)
+
+    for _ in range(max(args.warmup, 3)):
+        once()
+    barrier(world, device)
+    iters = max(10, min(200, args.steps))
+    st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    st.record()
+    for _ in range(iters):
+        once()
+    en.record()
+    torch.cuda.synchronize(device)
+    ms = max_over_ranks(st.elapsed_time(en) / iters, world, device)
+    kv_bytes = 2 * Bq * 8 * L * 128 * 2
+    return {"value": round(kv_bytes / (ms * 1e-3) / 1e9, 1), "unit": "GB/s", "ms_per_call": round(ms, 4),
+            "scaling": "strong", "batch": Bq, "kv_len": L, "per_gpu_kv_len": s1 - s0,
+            "collective": "none" if world == 1 else "one NCCL all_gather of packed fp32 (out, lse) partials"}
+
+
+def run_fmha_secondary(args, world, device, peaks) -> dict:
+    """Configs 3 and 4 on the tensor-core kernels (replicas: each rank its own batch)."""
+    from aicas_b200 import _native
+
+    caps = _native.capabilities()
+    out = {}
+    if not caps & _native.CAP_PREFILL_TCGEN05:
+        out["prefill_cfg4"] = {"unavailable": "tcgen05 prefill kernel not built in this library"}
+    else:
+        out["prefill_cfg4"] = time_prefill(args, world, device, peaks)
+    if not caps & _native.CAP_VARLEN_TCGEN05:
+        out["vit_cfg3"] = {"unavailable": "tcgen05 varlen kernel not built in this library"}
+    else:
+        out["vit_cfg3"] = time_varlen(args, world, device, peaks)
+    return out
+
+
+def _time_calls(fn, iters, warmup, world, device) -> float:
+    for _ in range(warmup):
+        fn()
+    barrier(world, device)
+    st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    st.record()
+    for _ in range(iters):
+        fn()
+    en.record()
+    torch.cuda.synchronize(device)
+    return max_over_ranks(st.elapsed_time(en) / iters, world, device)
+
+
+def time_prefill(args, world, device, peaks) -> dict:
+    import aicas_b200 as ab
+    from aicas_b200 import workloads as wl
+
+    q, k, v = wl.cfg4_prefill(seed=0, device=device)
+    flops = 2 * 8 * 16 * 2048 * 2048 * 128  # causal half of 4*S^2*D per (b, head)
+    ms = _time_calls(lambda: ab.gqa_flash_attention(q, k, v, causal=True, sm_scale=wl.SCALE_TEXT,
+                                                    num_key_value_groups=2), 20, 3, world, device)
+    tf = flops / (ms * 1e-3) / 1e12
+    return {"value": round(world * tf, 1), "unit": "TFLOP/s", "ms_per_call": round(ms, 4), "per_gpu_tflops": round(tf, 1),
+            "frac_of_bf16_peak": round(tf / peaks["bf16_tflops"], 4), "flops_per_call": flops,
+            "config": "B8 S2048 Hq16 Hkv8 D128 causal, MRoPE-rotated q/k", "scaling": "weak (replicas)"}
+
+
+def time_varlen(args, world, device, peaks) -> dict:
+    import aicas_b200 as ab
+    from aicas_b200 import workloads as wl
+
+    q, k, v, cu, lens = wl.cfg3_varlen(seed=0, device=device)
+    flops = sum(4 * n * n * 64 * 16 for n in lens)
+    ms = _time_calls(lambda: ab.varlen_flash_attention(q, k, v, cu_seq_lens_q=cu, cu_seq_lens_k=cu,
+                                                       sm_scale=wl.SCALE_VIT), 20, 3, world, device)
+    tf = flops / (ms * 1e-3) / 1e12
+    return {"value": round(world * tf, 1), "unit": "TFLOP/s", "ms_per_call": round(ms, 4), "per_gpu_tflops": round(tf, 1),
+            "frac_of_bf16_peak": round(tf / peaks["bf16_tflops"], 4), "flops_per_call": flops,
+            "config": f"32 images, grids U[16,64]^2, T={int(cu[-1])}, H16 D64, non-causal", "scaling": "weak (replicas)"}
+
+
+# ------------------------------------------------------------------ CPU (reference) path
+
+
+def cpu_decode_sample(target_s: float, max_layers: int = 100000) -> dict:
+    """Times the reference's CPU path (oracle/reference_cpu.py) on whole config-2
+    layers (all 64 requests) on the host cores; returns GB/s of the same metric."""
+    from aicas_b200 import workloads as wl
+    from oracle import reference_cpu as rc
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    lengths = wl.cfg2_lengths(0)
+    per_layer = step_bytes(lengths)["step"] / LAYERS
+    kc, vc = wl.cfg2_cache(B, L_CAP, 0, seed=0)
+    x = wl.cfg2_step_inputs(lengths, 0, seed=0)
+    rc.decode_layer(x.q, x.k, x.v, x.cos, x.sin, kc, vc, x.positions, wl.SCALE_TEXT)  # warm-up
+    layers, t0 = 0, time.perf_counter()
+    while layers < max_layers and (layers == 0 or time.perf_counter() - t0 < target_s):
+        rc.decode_layer(x.q, x.k, x.v, x.cos, x.sin, kc, vc, x.positions, wl.SCALE_TEXT)
+        layers += 1
+    dt = time.perf_counter() - t0
+    return {"value": round(layers * per_layer / dt / 1e9, 3), "unit": "GB/s", "cores": torch.get_num_threads(),
+            "kind": "port", "seconds": round(dt, 2),
+            "sample": f"{layers} x one config-2 layer (64 requests, RoPE + append + per-request SDPA) on CPU"}
+
+
+def run_reference(args, world, rank) -> dict | None:
+    if rank != 0:
+        return None
+    from aicas_b200 import workloads as wl
+    from oracle import reference_cpu as rc
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    lengths = wl.cfg2_lengths(0)
+    per_layer = step_bytes(lengths)["step"] / LAYERS
+    kc, vc = wl.cfg2_cache(B, L_CAP, 0, seed=0)
+    x = wl.cfg2_step_inputs(lengths, 0, seed=0)
+    def one_step():
+        for _ in range(LAYERS):
+            rc.decode_layer(x.q, x.k, x.v, x.cos, x.sin, kc, vc, x.positions, wl.SCALE_TEXT)
+
+    for _ in range(args.warmup):
+        one_step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        one_step()
+    dt = time.perf_counter() - t0
+    value = args.steps * LAYERS * per_layer / dt / 1e9
+    sample = ("one config-2 step per step: 28 layer calls (64 requests each: RoPE + cache append + per-request "
+              "SDPA, bf16) on CPU, layer 0's caches reused for every layer")
+    return {
+        "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(dt * 1e3 / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "impl": "reference",
+        "config": {"workload": "cfg2: batched GQA decode step (RoPE + KV append + decode) x 28 layers, reference CPU path",
+                   "batch": B, "kv_capacity": L_CAP, "lengths": "U[256,4096] seed 0"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+# ------------------------------------------------------------------ main
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-secondary", dest="secondary", action="store_false",
+                    help="skip the tensor-core prefill / ViT measurements")
+    ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        args.warmup = 3
+    world, rank, local = dist_info()
+    if world != args.gpus:
+        log(f"note: --gpus {args.gpus} but WORLD_SIZE={world}; using WORLD_SIZE")
+
+    if args.impl == "reference":
+        line = run_reference(args, world, rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return 0
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=180))
+    peaks, src = load_peaks()
+    line = run_ours(args, world, rank, device, peaks, src)
+    if rank == 0 and world == 1 and args.cpu_baseline:
+        line["cpu_baseline"] = cpu_decode_sample(target_s=10.0)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

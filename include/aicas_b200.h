@@ -1,0 +1,206 @@
+/*
+ * aicas_b200.h — C ABI of the B200 (sm_100a) attention backend for the
+ * Qwen3-VL-2B inference hot path.
+ *
+ * Every entry point takes plain pointers, sizes and element strides, launches
+ * on the caller's stream, allocates nothing, never synchronises the device and
+ * returns an int status (AICAS_OK on success).  On failure a message is kept in
+ * a thread-local buffer readable through aicas_last_error().
+ *
+ * The entry points replace these operators of the reference package
+ * `triton_qwen3vl` (paths relative to the reference project):
+ *
+ *   aicas_decode_gqa          triton_qwen3vl/gqa_decode_attention.py:268-327
+ *                             (_gqa_decode_attention_forward: q_len == 1 GQA
+ *                             decode returning out and a base-2 LSE), extended
+ *                             with a per-request length vector and split-KV
+ *   aicas_merge_partials      no single reference line: the (out, LSE) merge the
+ *                             reference never needed because it has no split-KV;
+ *                             it combines partials produced by aicas_decode_gqa
+ *                             on several devices (sequence-sharded caches)
+ *   aicas_prefill_gqa_causal  triton_qwen3vl/gqa_flash_attention.py:193-251
+ *                             (_gqa_flash_attention_forward, causal, q_len == kv_len)
+ *   aicas_varlen_attention    triton_qwen3vl/varlen_flash_attention.py:271-351
+ *                             (_varlen_flash_attention_forward, non-causal,
+ *                             packed sequences described by cu_seqlens)
+ *   aicas_rope_kv_append      HF apply_rotary_pos_emb (transformers
+ *                             models/qwen3_vl/modeling_qwen3_vl.py:410-432) followed by
+ *                             the in-place cache write of
+ *                             dujunbaoV1/evaluation_wrapper.py:84-100
+ *                             (InplaceDecodeCacheLayer.update); optional per-head
+ *                             RMSNorm as in dujunbaoV1/native_cuda_ops/
+ *                             decode_q1_gqa_kernel.cu:376-480
+ *
+ * Layout conventions: attention tensors are 4-D [batch, heads, tokens, head_dim]
+ * with head_dim contiguous (stride 1).  Strides are given in ELEMENTS.  All
+ * device pointers must be 16-byte aligned and every stride times the element
+ * size must be a multiple of 16 bytes.
+ */
+#ifndef AICAS_B200_H
+#define AICAS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define AICAS_API __attribute__((visibility("default")))
+#else
+#define AICAS_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define AICAS_ABI_VERSION 1
+
+/* element types */
+#define AICAS_DTYPE_F32 0
+#define AICAS_DTYPE_F16 1
+#define AICAS_DTYPE_BF16 2
+
+/* status codes */
+#define AICAS_OK 0
+#define AICAS_ERR_INVALID 1     /* malformed argument (null pointer, bad stride, ...) */
+#define AICAS_ERR_UNSUPPORTED 2 /* well-formed but outside what the kernels support */
+#define AICAS_ERR_CUDA 3        /* a CUDA runtime call failed */
+#define AICAS_ERR_WORKSPACE 4   /* workspace missing or too small */
+
+/* bits of the device-side error word (see aicas_device_error_flags) */
+#define AICAS_DEVERR_WAIT_TIMEOUT 1u /* a bounded barrier wait gave up */
+#define AICAS_DEVERR_TMEM 2u         /* tensor-memory allocation returned an unusable address */
+
+/* ------------------------------------------------------------------------ */
+/* GQA decode: one query token per request against that request's KV cache. */
+/* ------------------------------------------------------------------------ */
+typedef struct aicas_decode_params {
+  const void* q;           /* [B, Hq, 1, D] */
+  const void* k;           /* [B, Hkv, L, D]; consecutive tokens D elements apart */
+  const void* v;           /* [B, Hkv, L, D]; consecutive tokens D elements apart */
+  void* out;               /* [B, Hq, 1, D] same dtype as q; may be NULL if partial_o is set */
+  float* lse;              /* optional [B, Hq] fp32, base-2 log-sum-exp of the scaled logits
+                              (same convention as gqa_decode_attention.py:141) */
+  float* partial_o;        /* optional [B, Hq, D] fp32 normalised output, for a cross-device
+                              merge with aicas_merge_partials (lse must then be set too) */
+  const int32_t* kv_lens;  /* optional [B] valid cache length per request (0..L); NULL = L */
+  int64_t q_stride_b, q_stride_h;
+  int64_t k_stride_b, k_stride_h;
+  int64_t v_stride_b, v_stride_h;
+  int64_t o_stride_b, o_stride_h; /* strides of out (ignored when out is NULL) */
+  int32_t batch, num_q_heads, num_kv_heads, head_dim;
+  int32_t kv_capacity;     /* L: allocated cache length, upper bound of kv_lens */
+  int32_t dtype;           /* AICAS_DTYPE_* of q, k, v, out */
+  float sm_scale;
+  int32_t split_tokens;    /* tokens per split-KV work unit; 0 = choose automatically */
+} aicas_decode_params;
+
+/* Bytes of device workspace aicas_decode_gqa needs for these parameters.  The
+   workspace must be zero-filled once when it is allocated; every call leaves it
+   zero-filled again, so it can be reused (not concurrently) without clearing. */
+AICAS_API size_t aicas_decode_workspace_bytes(const aicas_decode_params* p);
+
+AICAS_API int aicas_decode_gqa(const aicas_decode_params* p, void* workspace, size_t workspace_bytes,
+                     void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Merge P partial (out, LSE) pairs into the final output.                   */
+/* ------------------------------------------------------------------------ */
+typedef struct aicas_merge_params {
+  const float* partial_o;   /* [P, B, H, D] fp32, contiguous */
+  const float* partial_lse; /* [P, B, H] fp32 base-2 LSE, contiguous */
+  void* out;                /* [B, H, D] (strided) */
+  float* lse;               /* optional [B, H] merged LSE */
+  int64_t o_stride_b, o_stride_h;
+  int32_t num_partials, batch, num_heads, head_dim;
+  int32_t dtype;            /* dtype of out */
+} aicas_merge_params;
+
+AICAS_API int aicas_merge_partials(const aicas_merge_params* p, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Flash attention on the tensor cores (tcgen05): causal GQA prefill and     */
+/* non-causal packed-varlen attention.                                       */
+/* ------------------------------------------------------------------------ */
+typedef struct aicas_fmha_params {
+  const void* q;            /* [B, Hq, Sq, D] */
+  const void* k;            /* [B, Hkv, Skv, D] */
+  const void* v;            /* [B, Hkv, Skv, D] */
+  void* out;                /* [B, Hq, Sq, D] */
+  int64_t q_stride_b, q_stride_h, q_stride_s;
+  int64_t k_stride_b, k_stride_h, k_stride_s;
+  int64_t v_stride_b, v_stride_h, v_stride_s;
+  int64_t o_stride_b, o_stride_h, o_stride_s;
+  int32_t batch, num_q_heads, num_kv_heads, seq_len_q, seq_len_kv, head_dim;
+  int32_t dtype;            /* AICAS_DTYPE_F16 or AICAS_DTYPE_BF16 */
+  float sm_scale;
+  const int32_t* cu_seqlens_q; /* varlen only: [num_seqs + 1] int32 on the device */
+  const int32_t* cu_seqlens_k; /* varlen only: [num_seqs + 1] int32 on the device */
+  int32_t num_seqs;            /* varlen only */
+} aicas_fmha_params;
+
+/* q_len == kv_len causal prefill, Hq a multiple of Hkv (gqa_flash_attention.py:12-46). */
+AICAS_API int aicas_prefill_gqa_causal(const aicas_fmha_params* p, void* stream);
+
+/* Block-diagonal non-causal attention over packed sequences, B == 1,
+   Hq == Hkv (varlen_flash_attention.py:58-99).  Reads cu_seqlens on the device:
+   no host synchronisation. */
+AICAS_API int aicas_varlen_attention(const aicas_fmha_params* p, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Fused (optional q/k RMSNorm) + RoPE + KV-cache append.                    */
+/* ------------------------------------------------------------------------ */
+typedef struct aicas_rope_append_params {
+  const void* q_in;         /* [B, Hq, S, D] */
+  void* q_out;              /* [B, Hq, S, D] rotated q (may alias q_in) */
+  const void* k_in;         /* [B, Hkv, S, D] new keys (before RoPE) */
+  const void* v_in;         /* [B, Hkv, S, D] new values */
+  const void* cos;          /* [B, S, D] */
+  const void* sin;          /* [B, S, D] */
+  void* k_cache;            /* [B, Hkv, C, D] */
+  void* v_cache;            /* [B, Hkv, C, D] */
+  const int32_t* positions; /* [B] slot of the first new token per request */
+  int32_t* kv_lens_out;     /* optional [B]: receives min(positions[b] + S, C) */
+  const void* q_norm_weight; /* optional [D] (dtype of q): per-head RMSNorm before RoPE */
+  const void* k_norm_weight; /* optional [D] */
+  float norm_eps;
+  int64_t qi_stride_b, qi_stride_h, qi_stride_s;
+  int64_t qo_stride_b, qo_stride_h, qo_stride_s;
+  int64_t k_stride_b, k_stride_h, k_stride_s;
+  int64_t v_stride_b, v_stride_h, v_stride_s;
+  int64_t cs_stride_b, cs_stride_s;  /* strides of cos and sin (same for both) */
+  int64_t kc_stride_b, kc_stride_h;  /* cache token stride is D */
+  int64_t vc_stride_b, vc_stride_h;
+  int32_t batch, num_q_heads, num_kv_heads, seq_len, head_dim, capacity;
+  int32_t dtype;            /* dtype of q, k, v, caches and norm weights */
+  int32_t cs_dtype;         /* dtype of cos/sin: same as dtype, or AICAS_DTYPE_F32 */
+} aicas_rope_append_params;
+
+AICAS_API int aicas_rope_kv_append(const aicas_rope_append_params* p, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Library queries.                                                           */
+/* ------------------------------------------------------------------------ */
+/* "aicas_b200 <version> sm_100a abi <n>" */
+AICAS_API const char* aicas_version(void);
+
+/* Bit set of AICAS_CAP_* features compiled into this library. */
+#define AICAS_CAP_DECODE 1u
+#define AICAS_CAP_MERGE 2u
+#define AICAS_CAP_PREFILL_TCGEN05 4u
+#define AICAS_CAP_VARLEN_TCGEN05 8u
+#define AICAS_CAP_ROPE_APPEND 16u
+AICAS_API uint32_t aicas_capabilities(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+AICAS_API const char* aicas_last_error(void);
+
+/* Reads (and optionally clears) the device-side error word of the current
+   device: AICAS_DEVERR_* bits set by kernels whose bounded waits gave up.
+   Synchronises the device; meant for tests and health checks, not hot loops. */
+AICAS_API int aicas_device_error_flags(uint32_t* flags, int clear);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AICAS_B200_H */

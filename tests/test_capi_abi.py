@@ -1,0 +1,165 @@
+"""The C-ABI library loads, exports exactly what include/aicas_b200.h declares,
+its structs have the layout the ctypes binding assumes, and argument
+validation rejects bad calls before anything reaches a GPU.  CPU only: no
+kernel is launched."""
+from __future__ import annotations
+
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+from aicas_b200 import _native as nat
+from tests.conftest import REPO
+
+HEADER = REPO / "include" / "aicas_b200.h"
+
+
+def declared_functions() -> set[str]:
+    text = HEADER.read_text()
+    return set(re.findall(r"AICAS_API\s+[\w\s\*]+?\b(aicas_\w+)\s*\(", text))
+
+
+def test_header_declares_the_binding_table():
+    assert declared_functions() == set(nat.EXPORTS)
+
+
+def test_library_exports_every_declared_symbol(native_lib):
+    out = subprocess.run(["nm", "-D", "--defined-only", str(nat.library_path())], capture_output=True, text=True,
+                         check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
+    assert declared_functions() <= exported
+    # nothing but the C ABI leaks out of the library
+    assert {s for s in exported if s.startswith("aicas")} == declared_functions()
+
+
+def test_version_and_capabilities(native_lib):
+    v = nat.version()
+    assert v.startswith("aicas_b200 ") and "sm_100a" in v
+    caps = nat.capabilities()
+    assert caps & nat.CAP_DECODE and caps & nat.CAP_MERGE and caps & nat.CAP_ROPE_APPEND
+
+
+STRUCTS = {
+    "aicas_decode_params": nat.DecodeParams,
+    "aicas_merge_params": nat.MergeParams,
+    "aicas_fmha_params": nat.FmhaParams,
+    "aicas_rope_append_params": nat.RopeAppendParams,
+}
+
+
+def test_struct_layouts_match_the_header(tmp_path: Path):
+    lines = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{HEADER}"', "int main(void) {"]
+    for cname, py in STRUCTS.items():
+        lines.append(f'  printf("{cname} size %zu\\n", sizeof({cname}));')
+        for fname, _ in py._fields_:
+            lines.append(f'  printf("{cname} {fname} %zu\\n", offsetof({cname}, {fname}));')
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-std=c11", "-o", str(exe), str(src)], check=True)
+    got = {}
+    for line in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.splitlines():
+        struct, field, value = line.split()
+        got[(struct, field)] = int(value)
+    for cname, py in STRUCTS.items():
+        assert got[(cname, "size")] == ctypes.sizeof(py), cname
+        for fname, _ in py._fields_:
+            assert got[(cname, fname)] == getattr(py, fname).offset, (cname, fname)
+
+
+def _decode_params(**over) -> nat.DecodeParams:
+    p = nat.DecodeParams()
+    base = 1 << 20  # fake, 16-byte aligned; never dereferenced: validation fails first or only sizes are computed
+    p.q, p.k, p.v, p.out = base, base * 2, base * 3, base * 4
+    p.batch, p.num_q_heads, p.num_kv_heads, p.head_dim = 64, 16, 8, 128
+    p.kv_capacity, p.dtype, p.sm_scale = 4096, nat.DTYPE_BF16, 128 ** -0.5
+    p.q_stride_b, p.q_stride_h = 16 * 128, 128
+    p.k_stride_b, p.k_stride_h = 8 * 4096 * 128, 4096 * 128
+    p.v_stride_b, p.v_stride_h = 8 * 4096 * 128, 4096 * 128
+    p.o_stride_b, p.o_stride_h = 16 * 128, 128
+    for k, v in over.items():
+        setattr(p, k, v)
+    return p
+
+
+@pytest.mark.parametrize(
+    "over, code, text",
+    [
+        ({"num_q_heads": 24}, nat.ERR_UNSUPPORTED, "group size 3"),
+        ({"num_q_heads": 12}, nat.ERR_INVALID, "not a multiple"),
+        ({"head_dim": 96}, nat.ERR_UNSUPPORTED, "head_dim 96"),
+        ({"dtype": 7}, nat.ERR_UNSUPPORTED, "dtype"),
+        ({"q": (1 << 20) + 2}, nat.ERR_INVALID, "aligned"),
+        ({"k_stride_h": 4096 * 128 + 4}, nat.ERR_INVALID, "16 bytes"),
+        ({"out": None}, nat.ERR_INVALID, "out / partial_o"),
+        ({"split_tokens": 100}, nat.ERR_UNSUPPORTED, "split_tokens"),
+        ({"batch": 0}, nat.ERR_INVALID, "batch=0"),
+    ],
+)
+def test_decode_validation(native_lib, over, code, text):
+    p = _decode_params(**over)
+    rc = native_lib.aicas_decode_gqa(ctypes.byref(p), None, 0, None)
+    assert rc == code
+    assert text in nat.last_error()
+    with pytest.raises(ValueError):
+        nat.check(rc, "aicas_decode_gqa")
+
+
+def test_decode_workspace_is_required_for_split_kv(native_lib):
+    p = _decode_params()
+    need = native_lib.aicas_decode_workspace_bytes(ctypes.byref(p))
+    assert need > 0
+    rc = native_lib.aicas_decode_gqa(ctypes.byref(p), None, 0, None)
+    assert rc == nat.ERR_WORKSPACE and str(need) in nat.last_error()
+
+
+def test_decode_workspace_size_formula(native_lib):
+    # split_tokens fixed -> max_splits = ceil(4096 / 512) = 8
+    p = _decode_params(split_tokens=512)
+    units, splits, g, d = 64 * 8, 8, 2, 128
+
+    def up(x):
+        return (x + 255) // 256 * 256
+
+    expect = up(units * splits * g * d * 4)
+    expect = up(expect + units * splits * g * 4)
+    expect = up(expect + units * 4)
+    assert native_lib.aicas_decode_workspace_bytes(ctypes.byref(p)) == expect
+    # a single split needs no workspace
+    assert native_lib.aicas_decode_workspace_bytes(ctypes.byref(_decode_params(split_tokens=4096))) == 0
+
+
+def test_fmha_validation(native_lib):
+    p = nat.FmhaParams()
+    p.q = p.k = p.v = p.out = 1 << 20
+    p.batch, p.num_q_heads, p.num_kv_heads, p.seq_len_q, p.seq_len_kv, p.head_dim = 1, 16, 8, 128, 128, 128
+    p.dtype = nat.DTYPE_F32
+    assert native_lib.aicas_prefill_gqa_causal(ctypes.byref(p), None) == nat.ERR_UNSUPPORTED
+    p.dtype = nat.DTYPE_BF16
+    p.seq_len_kv = 64
+    assert native_lib.aicas_prefill_gqa_causal(ctypes.byref(p), None) == nat.ERR_UNSUPPORTED
+    assert "q_len == kv_len" in nat.last_error()
+    p.seq_len_kv = 128
+    p.head_dim = 32
+    assert native_lib.aicas_prefill_gqa_causal(ctypes.byref(p), None) == nat.ERR_UNSUPPORTED
+    p.head_dim = 64
+    assert native_lib.aicas_varlen_attention(ctypes.byref(p), None) == nat.ERR_UNSUPPORTED  # batch ok, Hq != Hkv
+    assert "Hq == Hkv" in nat.last_error()
+    p.num_kv_heads = 16
+    assert native_lib.aicas_varlen_attention(ctypes.byref(p), None) == nat.ERR_INVALID  # no cu_seqlens
+    assert native_lib.aicas_prefill_gqa_causal(None, None) == nat.ERR_INVALID
+
+
+def test_rope_append_validation(native_lib):
+    p = nat.RopeAppendParams()
+    assert native_lib.aicas_rope_kv_append(ctypes.byref(p), None) == nat.ERR_INVALID
+    assert "must be set" in nat.last_error()
+
+
+def test_merge_validation(native_lib):
+    p = nat.MergeParams()
+    assert native_lib.aicas_merge_partials(ctypes.byref(p), None) == nat.ERR_INVALID

@@ -1,0 +1,129 @@
+"""Pins the CPU oracle against the golden vectors produced by running the
+reference itself (tests/golden/make_golden.py).  CPU only."""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from aicas_b200 import workloads as wl
+from oracle import attention as oa
+from oracle import cache as oc
+from oracle import rope as orope
+from tests.conftest import checksum, load_golden
+
+TIGHT = dict(rtol=0, atol=2e-6)
+
+
+def test_reference_prefill_seed0():
+    meta, a = load_golden("ref_prefill_seed0")
+    out = oa.sdpa(a["q"], a["k"], a["v"], meta["scale"], True, meta["groups"])
+    np.testing.assert_allclose(out.transpose(0, 2, 1, 3), a["out"], **TIGHT)
+
+
+def test_reference_decode_seed1_odd_length():
+    meta, a = load_golden("ref_decode_seed1")
+    assert a["k"].shape[2] == 65
+    out = oa.sdpa(a["q"], a["k"], a["v"], meta["scale"], False, meta["groups"])
+    np.testing.assert_allclose(out.transpose(0, 2, 1, 3), a["out"], **TIGHT)
+
+
+def test_reference_varlen_seed2():
+    meta, a = load_golden("ref_varlen_seed2")
+    out = oa.varlen(a["q"], a["k"], a["v"], a["cu"], a["cu"], meta["scale"])
+    np.testing.assert_allclose(out.transpose(0, 2, 1, 3), a["out"], **TIGHT)
+
+
+def test_cfg1_decode_fp32():
+    meta, a = load_golden("cfg1_decode")
+    q, k, v = wl.cfg1_decode(meta["seed"])
+    np.testing.assert_allclose(checksum(q, k, v), a["checksum"], rtol=1e-12)
+    out = oa.sdpa(q.numpy(), k.numpy(), v.numpy(), meta["scale"], False, meta["groups"])
+    np.testing.assert_allclose(out.transpose(0, 2, 1, 3), a["out"], **TIGHT)
+
+
+def test_cfg2_ragged_lengths():
+    meta, a = load_golden("cfg2_ragged_small")
+    g = wl.generator(meta["seed"])
+    q = wl.randn((4, wl.HQ, 1, wl.HEAD_DIM), g, torch.bfloat16)
+    kc = wl.randn((4, wl.HKV, meta["cap"], wl.HEAD_DIM), g, torch.bfloat16)
+    vc = wl.randn((4, wl.HKV, meta["cap"], wl.HEAD_DIM), g, torch.bfloat16)
+    np.testing.assert_allclose(checksum(q, kc, vc), a["checksum"], rtol=1e-12)
+    out = oa.decode_ragged(q.float().numpy(), kc.float().numpy(), vc.float().numpy(), meta["lens"], meta["scale"], 2)
+    np.testing.assert_allclose(out.transpose(0, 2, 1, 3), a["out"], **TIGHT)
+
+
+def test_cfg4_prefill_with_mrope():
+    meta, a = load_golden("cfg4_prefill_small")
+    q, k, v = wl.cfg4_prefill(seed=meta["seed"], batch=meta["batch"], seq=meta["seq"], hq=meta["hq"], hkv=meta["hkv"])
+    np.testing.assert_allclose(checksum(q, k, v), a["checksum"], rtol=1e-12)
+    out = oa.sdpa(q.float().numpy(), k.float().numpy(), v.float().numpy(), meta["scale"], True, meta["groups"])
+    np.testing.assert_allclose(out.transpose(0, 2, 1, 3), a["out"], **TIGHT)
+
+
+def test_cfg3_varlen():
+    meta, a = load_golden("cfg3_varlen_small")
+    q, k, v, cu, _ = wl.cfg3_varlen(seed=meta["seed"], images=meta["images"], heads=meta["heads"],
+                                    lo=meta["lo"], hi=meta["hi"])
+    np.testing.assert_allclose(checksum(q, k, v), a["checksum"], rtol=1e-12)
+    np.testing.assert_array_equal(cu.numpy(), a["cu"])
+    out = oa.varlen(q.float().numpy(), k.float().numpy(), v.float().numpy(), a["cu"], a["cu"], meta["scale"])
+    np.testing.assert_allclose(out.transpose(0, 2, 1, 3), a["out"], **TIGHT)
+
+
+def test_rope_bit_exact_against_hf():
+    meta, a = load_golden("rope_hf")
+    np.testing.assert_array_equal(orope.apply_rope(a["q"], a["cos"], a["sin"], "bf16"), a["q_rot"])
+    np.testing.assert_array_equal(orope.apply_rope(a["k"], a["cos"], a["sin"], "bf16"), a["k_rot"])
+
+
+def test_mrope_tables_match_hf():
+    meta, a = load_golden("rope_hf")
+    cos, sin = orope.mrope_cos_sin(a["position_ids"], 128, meta["theta"], meta["mrope_section"], "bf16")
+    # cos/sin of float32 arguments may differ by an ulp between libm implementations
+    np.testing.assert_allclose(cos, a["cos"], rtol=0, atol=2 ** -8)
+    np.testing.assert_allclose(sin, a["sin"], rtol=0, atol=2 ** -8)
+    assert (cos == a["cos"]).mean() > 0.99 and (sin == a["sin"]).mean() > 0.99
+
+
+def test_workload_mrope_tables_match_hf():
+    meta, a = load_golden("rope_hf")
+    cos, sin = wl.mrope_cos_sin(torch.from_numpy(a["position_ids"]), torch.bfloat16)
+    np.testing.assert_array_equal(cos.float().numpy(), a["cos"])
+    np.testing.assert_array_equal(sin.float().numpy(), a["sin"])
+
+
+def test_rms_norm_then_rope_against_hf():
+    meta, a = load_golden("rope_hf")
+    qn = orope.rms_norm_heads(a["q"], a["q_norm_w"], meta["eps"], "bf16")
+    kn = orope.rms_norm_heads(a["k"], a["k_norm_w"], meta["eps"], "bf16")
+    q = orope.apply_rope(qn, a["cos"], a["sin"], "bf16")
+    k = orope.apply_rope(kn, a["cos"], a["sin"], "bf16")
+    # the fp32 sum of squares may round differently from torch's reduction order
+    for got, ref in ((q, a["q_norm_rot"]), (k, a["k_norm_rot"])):
+        assert np.abs(got - ref).max() <= 2 ** -6 * max(1.0, np.abs(ref).max())
+        assert (got == ref).mean() > 0.98
+
+
+def test_kv_append_matches_inplace_cache_layer():
+    meta, a = load_golden("cache_append")
+    cap = meta["max_cache_len"]
+    kc = np.zeros_like(a["s0_k_cache"])
+    vc = np.zeros_like(a["s0_v_cache"])
+    for i, st in enumerate(meta["steps"]):
+        positions = [st["start"]] * kc.shape[0]
+        kc, vc, lens = oc.kv_append(kc, vc, a[f"s{i}_k_new"], a[f"s{i}_v_new"], positions)
+        np.testing.assert_array_equal(kc, a[f"s{i}_k_cache"])
+        np.testing.assert_array_equal(vc, a[f"s{i}_v_cache"])
+        assert (lens == st["visible"]).all() and st["visible"] <= cap
+
+
+def test_merge_of_sharded_partials_equals_full():
+    q, k, v = wl.cfg1_decode(0)
+    full = oa.sdpa(q.numpy(), k.numpy(), v.numpy(), wl.SCALE_TEXT, False, 2)[:, :, 0]
+    for shards in (2, 4, 8):
+        po, pl = oa.sharded_decode_partials(q.numpy(), k.numpy(), v.numpy(), wl.SCALE_TEXT, 2, shards)
+        np.testing.assert_allclose(oa.merge(po, pl), full, rtol=0, atol=1e-12)
+    lse = oa.lse_base2(q.numpy(), k.numpy(), wl.SCALE_TEXT, 2)
+    po, pl = oa.sharded_decode_partials(q.numpy(), k.numpy(), v.numpy(), wl.SCALE_TEXT, 2, 4)
+    m = pl.max(0)
+    np.testing.assert_allclose(m + np.log2(np.exp2(pl - m).sum(0)), lse, rtol=0, atol=1e-10)
