@@ -83,6 +83,10 @@ unsigned int* device_error_word() {
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+// Split-KV workspace: [counters: kMaxSplitUnits x u32][partial o][partial lse].
+constexpr int kMaxSplitUnits = 262144;
+constexpr size_t kCounterBytes = (size_t)kMaxSplitUnits * sizeof(unsigned int);
+
 // Split-KV plan shared by aicas_decode_workspace_bytes and aicas_decode_gqa.
 struct DecodePlan {
   int split_tokens;
@@ -111,13 +115,18 @@ int plan_decode(const aicas_decode_params* p, DecodePlan* out) {
   out->max_splits = (cap + split - 1) / split;
   const int g = p->num_q_heads / p->num_kv_heads;
   const size_t units = (size_t)p->batch * p->num_kv_heads;
-  size_t off = 0;
+  if (out->max_splits > 1 && units > kMaxSplitUnits)
+    return fail(AICAS_ERR_UNSUPPORTED, "split-KV decode supports at most %d (request, KV head) pairs (got %zu)",
+                kMaxSplitUnits, units);
+  // Counters live at a FIXED place (the first kCounterBytes) whatever the call's
+  // shape, so the zeros one call leaves behind are where the next call, of any
+  // shape, looks for them; partial results only ever go after that region.
+  size_t off = kCounterBytes;
+  out->ws_count_off = 0;
   out->ws_o_off = off;
   off = align_up(off + units * out->max_splits * g * p->head_dim * sizeof(float), 256);
   out->ws_lse_off = off;
   off = align_up(off + units * out->max_splits * g * sizeof(float), 256);
-  out->ws_count_off = off;
-  off = align_up(off + units * sizeof(unsigned int), 256);
   out->ws_bytes = out->max_splits > 1 ? off : 0;
   return AICAS_OK;
 }

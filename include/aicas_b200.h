@@ -94,9 +94,14 @@ typedef struct aicas_decode_params {
   int32_t split_tokens;    /* tokens per split-KV work unit; 0 = choose automatically */
 } aicas_decode_params;
 
-/* Bytes of device workspace aicas_decode_gqa needs for these parameters.  The
-   workspace must be zero-filled once when it is allocated; every call leaves it
-   zero-filled again, so it can be reused (not concurrently) without clearing. */
+/* Bytes of device workspace aicas_decode_gqa needs for these parameters (0 when
+   every request fits one split).  Layout: split counters in the first 1 MiB
+   (one uint32 per (request, KV head), at most 262144 pairs), then fp32 partial
+   outputs and LSEs.  Zero-fill the workspace once when it is allocated: every
+   completed call leaves the counter region zeroed again, so one buffer can be
+   reused by later calls of any shape on the same stream without clearing.
+   Calls that may overlap on the device need separate workspaces.  After a
+   device error (aicas_device_error_flags != 0) zero-fill it again. */
 AICAS_API size_t aicas_decode_workspace_bytes(const aicas_decode_params* p);
 
 AICAS_API int aicas_decode_gqa(const aicas_decode_params* p, void* workspace, size_t workspace_bytes,

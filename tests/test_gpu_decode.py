@@ -78,6 +78,21 @@ def test_decode_shapes_against_oracle(cuda_device, dtype, head_dim, groups):
         np.testing.assert_allclose(_np(lse[b : b + 1]), ref_lse, rtol=0, atol=1e-3)
 
 
+def test_workspace_reuse_across_shapes(cuda_device):
+    """One workspace serves calls of different shapes and split sizes in a row:
+    the split counters sit at a fixed offset and every call leaves them zeroed."""
+    torch.manual_seed(8)
+    cases = [(4, 2, 320, 64), (2, 8, 4096, 128), (4, 2, 320, 128), (64, 8, 512, 64), (4, 2, 320, 0), (1, 8, 2000, 64)]
+    for batch, hkv, L, split in cases * 2:
+        q = torch.randn(batch, hkv * 2, 1, 128, dtype=torch.bfloat16, device=cuda_device)
+        k = torch.randn(batch, hkv, L, 128, dtype=torch.bfloat16, device=cuda_device)
+        v = torch.randn_like(k)
+        lens = torch.randint(1, L + 1, (batch,)).tolist()
+        out = ab.gqa_decode_attention(q, k, v, sm_scale=0.09, num_key_value_groups=2, kv_lens=lens,
+                                      split_tokens=split)
+        bf16_tolerance_check(_np(out), oa.decode_ragged(_np(q), _np(k), _np(v), lens, 0.09, 2))
+
+
 def test_zero_and_full_lengths(cuda_device):
     torch.manual_seed(3)
     q = torch.randn(3, 16, 1, 128, dtype=torch.bfloat16, device=cuda_device)
