@@ -1,10 +1,612 @@
+// Flash-attention forward on the sm_100a tensor cores: causal GQA prefill and
+// non-causal packed-varlen (ViT) attention.
+//
+// Replaces the reference's Triton kernels
+//   triton_qwen3vl/gqa_flash_attention.py:79-190   (_gqa_flash_attention_fwd)
+//   triton_qwen3vl/varlen_flash_attention.py:149-264 (_varlen_flash_attention_fwd)
+// with the same math: S = Q K^T, online softmax in base 2 with fp32 statistics,
+// P rounded to the input dtype before P V (gqa_flash_attention.py:178), O / l.
+//
+// One CTA owns two 128-row query tiles that read the SAME key/value head:
+// the two query heads of a GQA pair (same rows), or two consecutive row blocks
+// of one head.  Each K/V tile is therefore loaded once for 256 query rows.
+//   warp 0      TMA producer: Q tiles once, then K_j, V_j through a stage ring
+//   warp 1      TMEM allocator and the single MMA-issuing thread
+//   warps 4-7   softmax + epilogue of query tile 0 (one TMEM lane = one row)
+//   warps 8-11  softmax + epilogue of query tile 1
+// TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [256+D,256+2D).
+// The MMAs are issued in the order S(0,0) S(0,1) | PV(j,0) S(j+1,0) PV(j,1)
+// S(j+1,1) | ..., so while one softmax group works on its S tile the tensor
+// core runs the other tile's products.  The O rescale is lazy: the reference
+// maximum only moves when a row's maximum grows by more than 2^8.
+//
+// Varlen scheduling is derived on the device from cu_seqlens (no host
+// metadata, no host synchronisation), unlike varlen_flash_attention.py:102-144.
+#include <cuda.h>
+
 #include <cstdio>
+#include <cstring>
+#include <type_traits>
+
+#include "common.cuh"
 #include "fmha.cuh"
+#include "tcgen05.cuh"
 
 namespace aicas {
-uint32_t fmha_capabilities() { return 0u; }
-int run_fmha(const aicas_fmha_params*, bool, cudaStream_t, unsigned int*, char* err, size_t errlen) {
-  snprintf(err, errlen, "tensor-core attention is not built yet");
-  return AICAS_ERR_UNSUPPORTED;
+namespace {
+
+constexpr int kBM = 128;  // query rows per tile (MMA M)
+constexpr int kBN = 128;  // keys per KV tile
+constexpr int kThreads = 384;
+
+struct FmhaArgs {
+  CUtensorMap tm_q, tm_k, tm_v;  // 4-D, box {64 elements, 128 rows, 1 head, 1 batch}
+  void* out;
+  int64_t o_sb, o_sh, o_ss;
+  int q_rows_first, k_rows_first, v_rows_first;  // 1: map dims (D, rows, heads, B); 0: (D, heads, rows, B)
+  int batch, hq, hkv, seq_q, seq_kv, group;
+  int pair_heads;  // 1: the two tiles are two heads of one KV group; 0: two row blocks of one head
+  int num_m;       // prefill: row blocks (of 128 rows if pair_heads else 256)
+  int num_units;   // prefill: CTAs per row block
+  float scale_log2;
+  const int32_t* cu_q;
+  const int32_t* cu_k;
+  int num_seqs;
+  unsigned int* err;
+};
+
+template <int D>
+struct Layout {
+  static constexpr uint32_t kQTile = kBM * D * 2;
+  static constexpr uint32_t kKVTile = kBN * D * 2;
+  static constexpr uint32_t kPTile = kBM * kBN * 2;
+  static constexpr int kStages = D == 128 ? 3 : 8;
+  static constexpr uint32_t kQ = 0;
+  static constexpr uint32_t kP = kQ + 2 * kQTile;
+  static constexpr uint32_t kKV = kP + 2 * kPTile;
+  static constexpr uint32_t kBar = kKV + kStages * kKVTile;
+  static constexpr int kNumBars = 1 + 2 * kStages + 6 + 1;
+  static constexpr uint32_t kMisc = kBar + kNumBars * 8;  // [tmem base][abort][schedule x 8]
+  static constexpr uint32_t kBytes = kMisc + 64 + 1024;   // + slack to align the base to 1024
+  static_assert(kBytes <= 232448, "shared memory budget");
+};
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  } else {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+}
+
+__device__ __forceinline__ void tma_tile(uint32_t dst, const CUtensorMap* map, int rows_first, int d0, int row,
+                                         int head, int b, uint32_t bar) {
+  if (rows_first) tma_load_4d(dst, map, d0, row, head, b, bar);
+  else tma_load_4d(dst, map, d0, head, row, b, bar);
+}
+
+// Every lane waits; the warp proceeds only if all lanes saw the phase.
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort, unsigned int* err) {
+  const bool ok = mbar_wait(bar, parity, abort, err);
+  return __all_sync(0xffffffffu, ok);
+}
+
+template <typename T, int D, bool CAUSAL, bool VARLEN>
+__global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_constant__ FmhaArgs a) {
+  using Lay = Layout<D>;
+  constexpr int NS = Lay::kStages;
+  constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t sb = (raw + 1023u) & ~1023u;
+  uint8_t* gb = smem_raw + (sb - raw);
+  const uint32_t bar0 = sb + Lay::kBar;
+  const uint32_t q_full = bar0;
+  auto kv_full = [&](int s) { return bar0 + 8u * (1 + s); };
+  auto kv_empty = [&](int s) { return bar0 + 8u * (1 + NS + s); };
+  auto s_full = [&](int t) { return bar0 + 8u * (1 + 2 * NS + t); };
+  auto p_full = [&](int t) { return bar0 + 8u * (3 + 2 * NS + t); };
+  auto o_full = [&](int t) { return bar0 + 8u * (5 + 2 * NS + t); };
+  const uint32_t mma_done = bar0 + 8u * (7 + 2 * NS);
+  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(gb + Lay::kMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(gb + Lay::kMisc + 4);
+  volatile int* sched = reinterpret_cast<volatile int*>(gb + Lay::kMisc + 8);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // ---------------------------------------------------------------- work unit
+  int b = 0, head0, head1, kvh, row0, row1, q_base = 0, k_base = 0, q_len, kv_len;
+  if constexpr (!VARLEN) {
+    const int L = blockIdx.x;
+    const int mb = a.num_m - 1 - L / a.num_units;  // longest causal rows first
+    const int u = L % a.num_units;
+    if (a.pair_heads) {
+      const int gp_per = a.group / 2;
+      const int per_b = a.hkv * gp_per;
+      b = u / per_b;
+      const int rem = u % per_b;
+      kvh = rem / gp_per;
+      head0 = kvh * a.group + 2 * (rem % gp_per);
+      head1 = head0 + 1;
+      row0 = row1 = mb * kBM;
+    } else {
+      b = u / a.hq;
+      head0 = head1 = u % a.hq;
+      kvh = head0 / a.group;
+      row0 = mb * 2 * kBM;
+      row1 = row0 + kBM;
+    }
+    q_len = kv_len = a.seq_q;
+  } else {
+    if (warp == 0) {
+      // find (sequence, row-pair block) of this CTA: prefix sums of
+      // ceil(len_q / 256) over the sequences, 32 sequences per step
+      const int H = a.hq;
+      int target = blockIdx.x / H;
+      int found = -1, pr = 0, qs = 0, ql = 0, ks = 0, kl = 0;
+      for (int base = 0; base < a.num_seqs && found < 0; base += 32) {
+        const int i = base + lane;
+        int np = 0, qsi = 0, qei = 0, ksi = 0, kei = 0;
+        if (i < a.num_seqs) {
+          qsi = min(max(a.cu_q[i], 0), a.seq_q);
+          qei = min(max(a.cu_q[i + 1], qsi), a.seq_q);
+          ksi = min(max(a.cu_k[i], 0), a.seq_kv);
+          kei = min(max(a.cu_k[i + 1], ksi), a.seq_kv);
+          np = (qei - qsi + 2 * kBM - 1) / (2 * kBM);
+        }
+        int incl = np;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+          const int v = __shfl_up_sync(0xffffffffu, incl, off);
+          if (lane >= off) incl += v;
+        }
+        const int excl = incl - np;
+        const unsigned ball = __ballot_sync(0xffffffffu, i < a.num_seqs && target >= excl && target < incl);
+        if (ball) {
+          const int src = __ffs(ball) - 1;
+          found = base + src;
+          pr = target - __shfl_sync(0xffffffffu, excl, src);
+          qs = __shfl_sync(0xffffffffu, qsi, src);
+          ql = __shfl_sync(0xffffffffu, qei - qsi, src);
+          ks = __shfl_sync(0xffffffffu, ksi, src);
+          kl = __shfl_sync(0xffffffffu, kei - ksi, src);
+        } else {
+          target -= __shfl_sync(0xffffffffu, incl, 31);
+        }
+      }
+      if (lane == 0) {
+        sched[0] = found;
+        sched[1] = pr;
+        sched[2] = qs;
+        sched[3] = ql;
+        sched[4] = ks;
+        sched[5] = kl;
+      }
+    }
+    __syncthreads();
+    if (sched[0] < 0) return;  // past the last tile (uniform)
+    head0 = head1 = kvh = blockIdx.x % a.hq;
+    row0 = sched[1] * 2 * kBM;
+    row1 = row0 + kBM;
+    q_base = sched[2];
+    q_len = sched[3];
+    k_base = sched[4];
+    kv_len = sched[5];
+  }
+  int kv_end = kv_len;
+  if (CAUSAL) kv_end = min(kv_len, max(row0, row1) + kBM);
+  const int n_kv = (kv_end + kBN - 1) / kBN;
+
+  // ---------------------------------------------------------------- set-up
+  if (threadIdx.x == 0) {
+    *abort_flag = 0;
+    mbar_init(q_full, 1);
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(kv_full(s), 1);
+      mbar_init(kv_empty(s), 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(s_full(t), 1);
+      mbar_init(p_full(t), 128);
+      mbar_init(o_full(t), 1);
+    }
+    mbar_init(mma_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(sb + Lay::kMisc, 512);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+  if (threadIdx.x == 0 && (tmem & 0xFFFFu) != 0u) {  // a 512-column allocation starts at column 0
+    flag_device_error(a.err, AICAS_DEVERR_TMEM);
+    *abort_flag = 1;
+  }
+  __syncthreads();
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0 && !*abort_flag) {
+      tma_prefetch_desc(&a.tm_q);
+      tma_prefetch_desc(&a.tm_k);
+      tma_prefetch_desc(&a.tm_v);
+      mbar_arrive_expect_tx(q_full, 2 * Lay::kQTile);
+      for (int t = 0; t < 2; ++t)
+        for (int bx = 0; bx < D / 64; ++bx)
+          tma_tile(sb + Lay::kQ + t * Lay::kQTile + bx * (kBM * 128), &a.tm_q, a.q_rows_first, bx * 64,
+                   q_base + (t ? row1 : row0), t ? head1 : head0, b, q_full);
+      int issued = 0;
+      for (int idx = 0; idx < 2 * n_kv; ++idx) {
+        const int s = idx % NS, u = idx / NS;
+        if (u > 0 && !mbar_wait(kv_empty(s), (u - 1) & 1, abort_flag, a.err)) break;
+        const bool is_v = idx & 1;
+        const int j = idx >> 1;
+        mbar_arrive_expect_tx(kv_full(s), Lay::kKVTile);
+        for (int bx = 0; bx < D / 64; ++bx)
+          tma_tile(sb + Lay::kKV + s * Lay::kKVTile + bx * (kBN * 128), is_v ? &a.tm_v : &a.tm_k,
+                   is_v ? a.v_rows_first : a.k_rows_first, bx * 64, k_base + j * kBN, kvh, b, kv_full(s));
+        ++issued;
+      }
+      if (*abort_flag) {  // let our own copies land before the CTA can retire
+        mbar_wait(q_full, 0, nullptr, a.err);
+        for (int idx = max(0, issued - NS); idx < issued; ++idx)
+          mbar_wait(kv_full(idx % NS), (idx / NS) & 1, nullptr, a.err);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issue (one thread)
+    if (lane == 0) {
+      constexpr uint32_t kIdS = tc::idesc_f16(kBF16, kBM, kBN, false, false);
+      constexpr uint32_t kIdPV = tc::idesc_f16(kBF16, kBM, D, false, true);
+      auto issue_s = [&](int stage, int t) {
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t aa = sb + Lay::kQ + t * Lay::kQTile + (kk >> 2) * (kBM * 128) + (kk & 3) * 32;
+          const uint32_t bb = sb + Lay::kKV + stage * Lay::kKVTile + (kk >> 2) * (kBN * 128) + (kk & 3) * 32;
+          tc::mma_f16_ss(tmem + t * 128, tc::smem_desc_sw128(aa, 16, 1024), tc::smem_desc_sw128(bb, 16, 1024), kIdS,
+                         kk > 0);
+        }
+      };
+      auto issue_pv = [&](int j, int stage, int t) {
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          const uint32_t aa = sb + Lay::kP + t * Lay::kPTile + (kk >> 2) * (kBM * 128) + (kk & 3) * 32;
+          const uint32_t bb = sb + Lay::kKV + stage * Lay::kKVTile + kk * (16 * 128);
+          tc::mma_f16_ss(tmem + 256 + t * D, tc::smem_desc_sw128(aa, 16, 1024),
+                         tc::smem_desc_sw128(bb, kBN * 128, 1024), kIdPV, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = !*abort_flag && mbar_wait(q_full, 0, abort_flag, a.err);
+      if (ok && n_kv > 0) {
+        ok = mbar_wait(kv_full(0), 0, abort_flag, a.err);
+        if (ok) {
+          tc::fence_after_sync();
+          issue_s(0, 0);
+          tc::commit(s_full(0));
+          issue_s(0, 1);
+          tc::commit(s_full(1));
+          tc::commit(kv_empty(0));
+        }
+        for (int j = 0; ok && j < n_kv; ++j) {
+          const int iv = 2 * j + 1, ik = 2 * j + 2;
+          const int sv = iv % NS, sk = ik % NS;
+          ok = mbar_wait(kv_full(sv), (iv / NS) & 1, abort_flag, a.err) &&
+               mbar_wait(p_full(0), j & 1, abort_flag, a.err);
+          if (!ok) break;
+          tc::fence_after_sync();
+          issue_pv(j, sv, 0);
+          tc::commit(o_full(0));
+          const bool more = j + 1 < n_kv;
+          if (more) {
+            ok = mbar_wait(kv_full(sk), (ik / NS) & 1, abort_flag, a.err);
+            if (!ok) break;
+            tc::fence_after_sync();
+            issue_s(sk, 0);
+            tc::commit(s_full(0));
+          }
+          ok = mbar_wait(p_full(1), j & 1, abort_flag, a.err);
+          if (!ok) break;
+          tc::fence_after_sync();
+          issue_pv(j, sv, 1);
+          tc::commit(o_full(1));
+          tc::commit(kv_empty(sv));
+          if (more) {
+            issue_s(sk, 1);
+            tc::commit(s_full(1));
+            tc::commit(kv_empty(sk));
+          }
+        }
+      }
+      // all products issued so far have completed before the CTA tears down
+      tc::commit(mma_done);
+      mbar_wait(mma_done, 0, nullptr, a.err);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ softmax + epilogue
+    const int t = (warp - 4) >> 2;
+    const int qw = warp & 3;
+    const int r = qw * 32 + lane;
+    const int tile_row0 = t ? row1 : row0;
+    const int row = tile_row0 + r;
+    const bool row_valid = row < q_len;
+    const uint32_t tl = tmem + ((uint32_t)(qw * 32) << 16);
+    const uint32_t col_s = t * 128, col_o = 256 + t * D;
+    const float c = a.scale_log2;
+    float m_ref = -INFINITY, l = 0.f;
+    bool ok = !*abort_flag;
+    uint32_t v[64];
+    for (int j = 0; ok && j < n_kv; ++j) {
+      if (!warp_wait(s_full(t), j & 1, abort_flag, a.err)) {
+        ok = false;
+        break;
+      }
+      tc::fence_after_sync();
+      const int kv0 = j * kBN;
+      const bool mask = (kv0 + kBN > kv_len) || (CAUSAL && kv0 + kBN - 1 > tile_row0);
+      // pass 1: maximum of the scaled row
+      float mx = -INFINITY;
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2) {
+        tc::tmem_ld32(tl + col_s + 64 * h2, v);
+        tc::tmem_ld32(tl + col_s + 64 * h2 + 32, v + 32);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          float x = __uint_as_float(v[i]) * c;
+          if (mask) {
+            const int col = kv0 + 64 * h2 + i;
+            if (col >= kv_len || (CAUSAL && col > row)) x = -INFINITY;
+          }
+          mx = fmaxf(mx, x);
+        }
+      }
+      bool rescale = false;
+      float alpha = 1.f;
+      if (mx > m_ref + 8.f) {  // first finite maximum, or growth beyond 2^8: move the reference
+        alpha = (m_ref == -INFINITY) ? 0.f : ex2(m_ref - mx);
+        rescale = j > 0 && m_ref != -INFINITY;
+        l *= alpha;
+        m_ref = mx;
+      }
+      const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
+      // P smem and O are free once PV(j-1) of this tile has completed
+      if (j > 0) {
+        if (!warp_wait(o_full(t), (j - 1) & 1, abort_flag, a.err)) {
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
+      }
+      if (__any_sync(0xffffffffu, rescale)) {
+        const float f = rescale ? alpha : 1.f;
+#pragma unroll
+        for (int cc = 0; cc < D / 32; ++cc) {
+          tc::tmem_ld32(tl + col_o + 32 * cc, v);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * f);
+          tc::tmem_st32(tl + col_o + 32 * cc, v);
+        }
+        tc::tmem_wait_st();
+      }
+      // pass 2: P = 2^(s*c - m), bf16/fp16 into the K-major 128B-swizzled P tile
+      float rs = 0.f;
+      uint8_t* prow = gb + Lay::kP + t * Lay::kPTile + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2) {
+        tc::tmem_ld32(tl + col_s + 64 * h2, v);
+        tc::tmem_ld32(tl + col_s + 64 * h2 + 32, v + 32);
+        tc::tmem_wait_ld();
+        uint32_t pk[32];
+#pragma unroll
+        for (int i = 0; i < 64; i += 2) {
+          float s0 = __uint_as_float(v[i]), s1 = __uint_as_float(v[i + 1]);
+          float p0 = ex2(fmaf(s0, c, -m_use)), p1 = ex2(fmaf(s1, c, -m_use));
+          if (mask) {
+            const int col = kv0 + 64 * h2 + i;
+            if (col >= kv_len || (CAUSAL && col > row)) p0 = 0.f;
+            if (col + 1 >= kv_len || (CAUSAL && col + 1 > row)) p1 = 0.f;
+          }
+          rs += p0 + p1;
+          pk[i >> 1] = pack2<T>(p0, p1);
+        }
+        uint8_t* sub = prow + h2 * (kBM * 128);
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch)
+          *reinterpret_cast<uint4*>(sub + ((ch ^ (r & 7)) << 4)) =
+              make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
+      }
+      l += rs;
+      fence_proxy_async_smem();
+      tc::fence_before_sync();
+      mbar_arrive(p_full(t));
+    }
+    // epilogue: O / l -> global, one row per thread
+    T* orow = static_cast<T*>(a.out) + (int64_t)b * a.o_sb + (int64_t)(t ? head1 : head0) * a.o_sh +
+              (int64_t)(q_base + row) * a.o_ss;
+    if (ok && n_kv > 0) {
+      if (warp_wait(o_full(t), (n_kv - 1) & 1, abort_flag, a.err)) {
+        tc::fence_after_sync();
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll
+        for (int cc = 0; cc < D / 32; ++cc) {
+          tc::tmem_ld32(tl + col_o + 32 * cc, v);
+          tc::tmem_wait_ld();
+          if (row_valid) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              pk[i] = pack2<T>(__uint_as_float(v[2 * i]) * inv, __uint_as_float(v[2 * i + 1]) * inv);
+            uint4* dst = reinterpret_cast<uint4*>(orow + 32 * cc);
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4)
+              dst[q4] = make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
+          }
+        }
+      }
+    } else if (ok && row_valid) {
+      uint4* dst = reinterpret_cast<uint4*>(orow);
+      for (int q4 = 0; q4 < D / 8; ++q4) dst[q4] = make_uint4(0u, 0u, 0u, 0u);  // empty key range
+    }
+  }
+
+  // ---------------------------------------------------------------- teardown
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// 4-D map over [B, heads, rows, D] (element strides), the two middle dimensions
+// ordered by increasing stride as the tensor-map encoder expects.
+bool make_map(CUtensorMap* m, const void* ptr, bool bf16, int d, int rows, int heads, int batch, int64_t s_b,
+              int64_t s_h, int64_t s_s, int* rows_first, char* err, size_t errlen) {
+  EncodeTiledFn enc = encode_fn();
+  if (enc == nullptr) {
+    snprintf(err, errlen, "cuTensorMapEncodeTiled is unavailable from the driver");
+    return false;
+  }
+  // size-1 dimensions may carry any stride in a torch view: give them a valid one
+  const int64_t big = (int64_t)rows * s_s + (int64_t)heads * s_h + 8;
+  if (heads == 1) s_h = ((s_s * (int64_t)rows + 7) / 8) * 8;
+  if (rows == 1) s_s = ((s_h * (int64_t)heads + 7) / 8) * 8;
+  if (batch == 1) s_b = ((big + 7) / 8) * 8;
+  const bool rf = s_s <= s_h;
+  cuuint64_t dims[4], strides[3];
+  cuuint32_t box[4], estr[4] = {1, 1, 1, 1};
+  dims[0] = (cuuint64_t)d;
+  box[0] = 64;
+  if (rf) {
+    dims[1] = rows; dims[2] = heads; strides[0] = s_s * 2; strides[1] = s_h * 2; box[1] = 128; box[2] = 1;
+  } else {
+    dims[1] = heads; dims[2] = rows; strides[0] = s_h * 2; strides[1] = s_s * 2; box[1] = 1; box[2] = 128;
+  }
+  dims[3] = batch;
+  strides[2] = s_b * 2;
+  box[3] = 1;
+  CUresult r = enc(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+                   const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    snprintf(err, errlen, "cuTensorMapEncodeTiled failed (%d) for dims [%d,%d,%d,%d] strides [%lld,%lld,%lld]",
+             (int)r, d, rows, heads, batch, (long long)s_s, (long long)s_h, (long long)s_b);
+    return false;
+  }
+  *rows_first = rf ? 1 : 0;
+  return true;
+}
+
+template <typename T, int D, bool CAUSAL, bool VARLEN>
+cudaError_t launch_t(const FmhaArgs& a, int grid, cudaStream_t st) {
+  auto kern = fmha_fwd_kernel<T, D, CAUSAL, VARLEN>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Layout<D>::kBytes);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  kern<<<grid, kThreads, Layout<D>::kBytes, st>>>(a);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t dispatch(int d, bool varlen, const FmhaArgs& a, int grid, cudaStream_t st) {
+  if (d == 128) return varlen ? launch_t<T, 128, false, true>(a, grid, st) : launch_t<T, 128, true, false>(a, grid, st);
+  return varlen ? launch_t<T, 64, false, true>(a, grid, st) : launch_t<T, 64, true, false>(a, grid, st);
+}
+
+}  // namespace
+
+uint32_t fmha_capabilities() { return AICAS_CAP_PREFILL_TCGEN05 | AICAS_CAP_VARLEN_TCGEN05; }
+
+int run_fmha(const aicas_fmha_params* p, bool varlen, cudaStream_t stream, unsigned int* dev_err, char* err,
+             size_t errlen) {
+  if (p->seq_len_q == 0) return AICAS_OK;
+  const bool bf16 = p->dtype == AICAS_DTYPE_BF16;
+  FmhaArgs a;
+  memset(&a, 0, sizeof(a));
+  if (!make_map(&a.tm_q, p->q, bf16, p->head_dim, p->seq_len_q, p->num_q_heads, p->batch, p->q_stride_b,
+                p->q_stride_h, p->q_stride_s, &a.q_rows_first, err, errlen) ||
+      !make_map(&a.tm_k, p->k, bf16, p->head_dim, p->seq_len_kv, p->num_kv_heads, p->batch, p->k_stride_b,
+                p->k_stride_h, p->k_stride_s, &a.k_rows_first, err, errlen) ||
+      !make_map(&a.tm_v, p->v, bf16, p->head_dim, p->seq_len_kv, p->num_kv_heads, p->batch, p->v_stride_b,
+                p->v_stride_h, p->v_stride_s, &a.v_rows_first, err, errlen))
+    return AICAS_ERR_UNSUPPORTED;
+  a.out = p->out;
+  a.o_sb = p->o_stride_b;
+  a.o_sh = p->o_stride_h;
+  a.o_ss = p->o_stride_s;
+  a.batch = p->batch;
+  a.hq = p->num_q_heads;
+  a.hkv = p->num_kv_heads;
+  a.seq_q = p->seq_len_q;
+  a.seq_kv = p->seq_len_kv;
+  a.group = p->num_q_heads / p->num_kv_heads;
+  a.scale_log2 = p->sm_scale * 1.4426950408889634f;
+  a.err = dev_err;
+  long long grid;
+  if (varlen) {
+    a.cu_q = p->cu_seqlens_q;
+    a.cu_k = p->cu_seqlens_k;
+    a.num_seqs = p->num_seqs;
+    if (p->num_seqs == 0) return AICAS_OK;
+    grid = ((long long)(p->seq_len_q + 2 * kBM - 1) / (2 * kBM) + p->num_seqs) * p->num_q_heads;
+  } else {
+    a.pair_heads = (a.group % 2 == 0) ? 1 : 0;
+    a.num_m = a.pair_heads ? (p->seq_len_q + kBM - 1) / kBM : (p->seq_len_q + 2 * kBM - 1) / (2 * kBM);
+    a.num_units = a.pair_heads ? p->batch * p->num_kv_heads * (a.group / 2) : p->batch * p->num_q_heads;
+    grid = (long long)a.num_m * a.num_units;
+  }
+  if (grid > 0x7fffffffLL) {
+    snprintf(err, errlen, "attention grid too large");
+    return AICAS_ERR_UNSUPPORTED;
+  }
+  if (grid == 0) return AICAS_OK;
+  const cudaError_t e = bf16 ? dispatch<__nv_bfloat16>(p->head_dim, varlen, a, (int)grid, stream)
+                             : dispatch<__half>(p->head_dim, varlen, a, (int)grid, stream);
+  if (e != cudaSuccess) {
+    snprintf(err, errlen, "attention launch: %s (%s)", cudaGetErrorString(e), cudaGetErrorName(e));
+    return AICAS_ERR_CUDA;
+  }
+  return AICAS_OK;
+}
+
 }  // namespace aicas
