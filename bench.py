@@ -168,34 +168,35 @@ def barrier(world: int, device):
 # ------------------------------------------------------------------ workload
 
 
-def step_bytes(lengths: torch.Tensor) -> dict:
+def step_bytes(lengths: torch.Tensor, layers: int = LAYERS) -> dict:
     """Algorithmic bytes of one config-2 step (padded slots are not counted)."""
     hq, hkv, d, e = 16, 8, 128, 2
     kv = int(sum(2 * hkv * d * e * (int(n) + 1) for n in lengths))  # K and V of the valid prefix incl. the new token
     qo = 2 * B * hq * d * e                                         # decode reads q, writes o
     rope = B * (hq + 2 * hkv) * d * e + 2 * B * d * e + B * hq * d * e + 2 * B * hkv * d * e
-    return {"decode_per_layer": kv + qo, "rope_per_layer": rope, "step": LAYERS * (kv + qo + rope)}
+    return {"decode_per_layer": kv + qo, "rope_per_layer": rope, "step": layers * (kv + qo + rope)}
 
 
 class DecodeWorkload:
-    def __init__(self, device, seed: int):
+    def __init__(self, device, seed: int, layers: int = LAYERS):
         import aicas_b200 as ab
         from aicas_b200 import workloads as wl
 
         self.ab, self.wl = ab, wl
         self.device = device
+        self.layers = layers
         self.lengths = wl.cfg2_lengths(0)
-        self.caches = [wl.cfg2_cache(B, L_CAP, layer, seed=seed, device=device) for layer in range(LAYERS)]
-        self.inputs = [wl.cfg2_step_inputs(self.lengths, layer, seed=seed, device=device) for layer in range(LAYERS)]
+        self.caches = [wl.cfg2_cache(B, L_CAP, layer, seed=seed, device=device) for layer in range(layers)]
+        self.inputs = [wl.cfg2_step_inputs(self.lengths, layer, seed=seed, device=device) for layer in range(layers)]
         self.lens_after = torch.empty(B, dtype=torch.int32, device=device)
         self.q_rot = [torch.empty(B, 1, 16, 128, dtype=torch.bfloat16, device=device).transpose(1, 2)
-                      for _ in range(LAYERS)]
-        self.bytes = step_bytes(self.lengths)
+                      for _ in range(layers)]
+        self.bytes = step_bytes(self.lengths, layers)
 
     def step(self, decode_events=None):
         ab, wl = self.ab, self.wl
         outs = []
-        for layer in range(LAYERS):
+        for layer in range(self.layers):
             x = self.inputs[layer]
             kc, vc = self.caches[layer]
             ab.rope_kv_append(x.q, x.k, x.v, x.cos, x.sin, kc, vc, x.positions, q_out=self.q_rot[layer],
@@ -209,13 +210,9 @@ class DecodeWorkload:
         return outs
 
 
-def run_ours(args, world, rank, device, peaks, peak_src) -> dict | None:
-    import aicas_b200 as ab
-    from aicas_b200 import _native
-    from aicas_b200 import workloads as wl
-
-    _native.lib()  # loud failure if the library is missing
-    wk = DecodeWorkload(device, seed=rank)
+def run_decode(args, world, rank, device, peaks, peak_src) -> dict:
+    """The headline: config-2 decode steps replayed from one CUDA graph."""
+    wk = DecodeWorkload(device, seed=rank, layers=args.layers)
     torch.cuda.synchronize(device)
 
     # --- capture the 28-layer step (56 launches) in a CUDA graph, with timing
@@ -228,7 +225,7 @@ def run_ours(args, world, rank, device, peaks, peak_src) -> dict | None:
     torch.cuda.current_stream(device).wait_stream(cap_stream)
     torch.cuda.synchronize(device)
     def capture(with_events: bool):
-        ev = ([[torch.cuda.Event(enable_timing=True, external=True) for _ in range(2)] for _ in range(LAYERS)]
+        ev = ([[torch.cuda.Event(enable_timing=True, external=True) for _ in range(2)] for _ in range(wk.layers)]
               if with_events else None)
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=cap_stream):
@@ -265,7 +262,7 @@ def run_ours(args, world, rank, device, peaks, peak_src) -> dict | None:
         # the events hold the launches of the last timed replay (28 decode launches)
         dec_ms = [a.elapsed_time(b) for a, b in ev]
     else:
-        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(LAYERS)]
+        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(wk.layers)]
         wk.step(decode_events=ev)
         torch.cuda.synchronize(device)
         dec_ms = [a.elapsed_time(b) for a, b in ev]
@@ -278,35 +275,25 @@ def run_ours(args, world, rank, device, peaks, peak_src) -> dict | None:
                 "traffic": profiled_traffic("decode_gqa_cfg2.txt"),
                 "algorithmic_bytes_per_launch": wk.bytes["decode_per_layer"],
                 "avg_launch_us": round(dec_avg_ms * 1e3, 2),
-                "decode_share_of_step": round(dec_avg_ms * LAYERS / ms_step, 3)}
+                "decode_share_of_step": round(dec_avg_ms * wk.layers / ms_step, 3)}
     del graph
-
-    # --- end to end through the public API with host buffers (eager, no graph)
-    e2e = run_e2e(wk, args, world, device)
-
-    # --- secondary: config 5 split-KV across the ranks
-    split = run_split_kv(args, world, rank, device)
-    fmha = run_fmha_secondary(args, world, device, peaks) if args.secondary else {}
-    line = None
-    if rank == 0:
-        line = {
-            "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "cfg2: batched GQA decode step (RoPE + KV append + split-KV decode) x 28 layers",
-                       "batch_per_gpu": B, "layers": LAYERS, "q_heads": 16, "kv_heads": 8, "head_dim": 128,
-                       "kv_capacity": L_CAP, "lengths": "U[256,4096] seed 0", "mean_len": float(wk.lengths.float().mean()),
-                       "parallelism": f"dp{world} (requests sharded, no collective)",
-                       "l2": "inputs larger than L2 (571 MB of valid KV per layer, 30 GB resident)",
-                       "graph": "28-layer step captured in one CUDA graph (56 launches)"},
-            "roofline": roofline,
-            "e2e": e2e,
-            "gpu_launches": args.steps * LAYERS * 2,
-            "clocks": clocks.summary(),
-            "split_kv_cfg5": split,
-            **fmha,
-        }
-    return line
+    e2e = run_e2e(wk, args, world, device) if args.e2e else None
+    out = {
+        "value": round(value, 1), "ms_per_step": round(ms_step, 4),
+        "config": {"workload": f"cfg2: batched GQA decode step (RoPE + KV append + split-KV decode) x {wk.layers} layers",
+                   "batch_per_gpu": B, "layers": wk.layers, "q_heads": 16, "kv_heads": 8, "head_dim": 128,
+                   "kv_capacity": L_CAP, "lengths": "U[256,4096] seed 0",
+                   "mean_len": round(float(wk.lengths.float().mean()), 2),
+                   "parallelism": f"dp{world} (requests sharded, no collective)",
+                   "l2": "inputs larger than L2 (571 MB of valid KV per layer)",
+                   "graph": f"{wk.layers}-layer step captured in one CUDA graph ({2 * wk.layers} launches)"},
+        "roofline": roofline, "gpu_launches": args.steps * wk.layers * 2, "clocks": clocks.summary(),
+    }
+    if e2e is not None:
+        out["e2e"] = e2e
+    del wk
+    torch.cuda.empty_cache()
+    return out
 
 
 def run_e2e(wk: DecodeWorkload, args, world, device) -> dict:
@@ -322,13 +309,13 @@ def run_e2e(wk: DecodeWorkload, args, world, device) -> dict:
     host_in = []
     for x in wk.inputs:
         host_in.append([t.cpu().pin_memory() for t in (x.q, x.k, x.v, x.cos, x.sin, x.positions)])
-    host_out = [torch.empty(B, 1, 16, 128, dtype=torch.bfloat16).pin_memory() for _ in range(LAYERS)]
+    host_out = [torch.empty(B, 1, 16, 128, dtype=torch.bfloat16).pin_memory() for _ in range(wk.layers)]
     h2d = sum(t.numel() * t.element_size() for ts in host_in for t in ts)
     d2h = sum(t.numel() * t.element_size() for t in host_out)
     lens_after = torch.empty(B, dtype=torch.int32, device=device)
 
     def one_step():
-        for layer in range(LAYERS):
+        for layer in range(wk.layers):
             q, k, v, cos, sin, pos = (t.to(device, non_blocking=True) for t in host_in[layer])
             kc, vc = wk.caches[layer]
             q_rot = ab.rope_kv_append(q, k, v, cos, sin, kc, vc, pos, kv_lens_out=lens_after)
@@ -387,20 +374,22 @@ def run_split_kv(args, world, rank, device) -> dict:
             "collective": "none" if world == 1 else "one NCCL all_gather of packed fp32 (out, lse) partials"}
 
 
-def run_fmha_secondary(args, world, device, peaks) -> dict:
+def run_fmha_secondary(args, world, device, peaks, only=None) -> dict:
     """Configs 3 and 4 on the tensor-core kernels (replicas: each rank its own batch)."""
     from aicas_b200 import _native
 
     caps = _native.capabilities()
     out = {}
-    if not caps & _native.CAP_PREFILL_TCGEN05:
-        out["prefill_cfg4"] = {"unavailable": "tcgen05 prefill kernel not built in this library"}
-    else:
-        out["prefill_cfg4"] = time_prefill(args, world, device, peaks)
-    if not caps & _native.CAP_VARLEN_TCGEN05:
-        out["vit_cfg3"] = {"unavailable": "tcgen05 varlen kernel not built in this library"}
-    else:
-        out["vit_cfg3"] = time_varlen(args, world, device, peaks)
+    if only in (None, "prefill"):
+        if not caps & _native.CAP_PREFILL_TCGEN05:
+            out["prefill_cfg4"] = {"unavailable": "tcgen05 prefill kernel not built in this library"}
+        else:
+            out["prefill_cfg4"] = time_prefill(args, world, device, peaks)
+    if only in (None, "vit"):
+        if not caps & _native.CAP_VARLEN_TCGEN05:
+            out["vit_cfg3"] = {"unavailable": "tcgen05 varlen kernel not built in this library"}
+        else:
+            out["vit_cfg3"] = time_varlen(args, world, device, peaks)
     return out
 
 
@@ -518,6 +507,10 @@ def main(argv=None) -> int:
     ap.add_argument("--no-secondary", dest="secondary", action="store_false",
                     help="skip the tensor-core prefill / ViT measurements")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    ap.add_argument("--no-e2e", dest="e2e", action="store_false", help="skip the end-to-end host-buffer measurement")
+    ap.add_argument("--only", choices=["decode", "split_kv", "prefill", "vit"], default=None,
+                    help="run one workload (profiling)")
+    ap.add_argument("--layers", type=int, default=LAYERS, help="decode layers per step (28 = Qwen3-VL-2B)")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         args.warmup = 3
@@ -538,8 +531,30 @@ def main(argv=None) -> int:
 
         dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=180))
     peaks, src = load_peaks()
-    line = run_ours(args, world, rank, device, peaks, src)
-    if rank == 0 and world == 1 and args.cpu_baseline:
+    from aicas_b200 import _native
+
+    _native.lib()  # loud failure if the library is missing
+    only = args.only
+    result = {}
+    if only in (None, "decode"):
+        result["decode"] = run_decode(args, world, rank, device, peaks, src)
+    if only in (None, "split_kv"):
+        result["split_kv_cfg5"] = run_split_kv(args, world, rank, device)
+    if args.secondary and only in (None, "prefill", "vit"):
+        result.update(run_fmha_secondary(args, world, device, peaks, only))
+    line = None
+    if rank == 0:
+        line = {"metric": METRIC, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "higher_is_better": True, "vs_baseline": None, "dtype": "bf16", "data": "synthetic"}
+        dec = result.pop("decode", None)
+        if dec is not None:
+            line.update({"value": dec["value"], "unit": "GB/s", "ms_per_step": dec["ms_per_step"], "scaling": "weak",
+                         "config": dec["config"], "roofline": dec["roofline"], "e2e": dec.get("e2e"),
+                         "gpu_launches": dec["gpu_launches"], "clocks": dec["clocks"]})
+        else:
+            line.update({"value": None, "unit": None, "note": f"--only {only}: headline decode not run"})
+        line.update(result)
+    if rank == 0 and world == 1 and args.cpu_baseline and only in (None, "decode"):
         line["cpu_baseline"] = cpu_decode_sample(target_s=10.0)
     if world > 1:
         import torch.distributed as dist
