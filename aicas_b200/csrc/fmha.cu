@@ -65,7 +65,7 @@ struct Layout {
   static constexpr uint32_t kP = kQ + 2 * kQTile;
   static constexpr uint32_t kKV = kP + 2 * kPTile;
   static constexpr uint32_t kBar = kKV + kStages * kKVTile;
-  static constexpr int kNumBars = 1 + 2 * kStages + 6 + 1;
+  static constexpr int kNumBars = 1 + 2 * kStages + 8 + 1;
   static constexpr uint32_t kMisc = kBar + kNumBars * 8;  // [tmem base][abort][schedule x 8]
   static constexpr uint32_t kBytes = kMisc + 64 + 1024;   // + slack to align the base to 1024
   static_assert(kBytes <= 232448, "shared memory budget");
@@ -116,7 +116,8 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
   auto s_full = [&](int t) { return bar0 + 8u * (1 + 2 * NS + t); };
   auto p_full = [&](int t) { return bar0 + 8u * (3 + 2 * NS + t); };
   auto o_full = [&](int t) { return bar0 + 8u * (5 + 2 * NS + t); };
-  const uint32_t mma_done = bar0 + 8u * (7 + 2 * NS);
+  auto s_free = [&](int t) { return bar0 + 8u * (7 + 2 * NS + t); };
+  const uint32_t mma_done = bar0 + 8u * (9 + 2 * NS);
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(gb + Lay::kMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(gb + Lay::kMisc + 4);
   volatile int* sched = reinterpret_cast<volatile int*>(gb + Lay::kMisc + 8);
@@ -219,6 +220,7 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
       mbar_init(s_full(t), 1);
       mbar_init(p_full(t), 128);
       mbar_init(o_full(t), 1);
+      mbar_init(s_free(t), 128);
     }
     mbar_init(mma_done, 1);
     fence_mbar_init();
@@ -236,7 +238,6 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
     *abort_flag = 1;
   }
   __syncthreads();
-
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0 && !*abort_flag) {
@@ -300,22 +301,34 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
           tc::commit(s_full(1));
           tc::commit(kv_empty(0));
         }
+        // Steady state, in the order the softmax groups release their inputs:
+        // S(j+1,0) as soon as group 0 has READ S(j,0) (not after its softmax),
+        // PV(j,0) once P(j,0) is written, then the same for tile 1.
         for (int j = 0; ok && j < n_kv; ++j) {
           const int iv = 2 * j + 1, ik = 2 * j + 2;
           const int sv = iv % NS, sk = ik % NS;
+          const bool more = j + 1 < n_kv;
+          if (more) {
+            ok = mbar_wait(kv_full(sk), (ik / NS) & 1, abort_flag, a.err) &&
+                 mbar_wait(s_free(0), j & 1, abort_flag, a.err);
+            if (!ok) break;
+            tc::fence_after_sync();
+            issue_s(sk, 0);
+            tc::commit(s_full(0));
+          }
           ok = mbar_wait(kv_full(sv), (iv / NS) & 1, abort_flag, a.err) &&
                mbar_wait(p_full(0), j & 1, abort_flag, a.err);
           if (!ok) break;
           tc::fence_after_sync();
           issue_pv(j, sv, 0);
           tc::commit(o_full(0));
-          const bool more = j + 1 < n_kv;
           if (more) {
-            ok = mbar_wait(kv_full(sk), (ik / NS) & 1, abort_flag, a.err);
+            ok = mbar_wait(s_free(1), j & 1, abort_flag, a.err);
             if (!ok) break;
             tc::fence_after_sync();
-            issue_s(sk, 0);
-            tc::commit(s_full(0));
+            issue_s(sk, 1);
+            tc::commit(s_full(1));
+            tc::commit(kv_empty(sk));
           }
           ok = mbar_wait(p_full(1), j & 1, abort_flag, a.err);
           if (!ok) break;
@@ -323,11 +336,6 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
           issue_pv(j, sv, 1);
           tc::commit(o_full(1));
           tc::commit(kv_empty(sv));
-          if (more) {
-            issue_s(sk, 1);
-            tc::commit(s_full(1));
-            tc::commit(kv_empty(sk));
-          }
         }
       }
       // all products issued so far have completed before the CTA tears down
@@ -347,31 +355,45 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
     const float c = a.scale_log2;
     float m_ref = -INFINITY, l = 0.f;
     bool ok = !*abort_flag;
-    uint32_t v[64];
+    uint32_t v[128];  // the S row of this thread, then reused for O chunks
+    const uint32_t masked_bits = __float_as_uint(c >= 0.f ? -INFINITY : INFINITY);  // s*c -> -inf
     for (int j = 0; ok && j < n_kv; ++j) {
       if (!warp_wait(s_full(t), j & 1, abort_flag, a.err)) {
         ok = false;
         break;
       }
       tc::fence_after_sync();
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) tc::tmem_ld32(tl + col_s + 32 * cc, v + 32 * cc);
+      tc::tmem_wait_ld();
+      // S(j) is in registers: the tensor core may overwrite it with S(j+1) now
+      tc::fence_before_sync();
+      mbar_arrive(s_free(t));
       const int kv0 = j * kBN;
       const bool mask = (kv0 + kBN > kv_len) || (CAUSAL && kv0 + kBN - 1 > tile_row0);
-      // pass 1: maximum of the scaled row
-      float mx = -INFINITY;
+      if (mask) {
 #pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
-        tc::tmem_ld32(tl + col_s + 64 * h2, v);
-        tc::tmem_ld32(tl + col_s + 64 * h2 + 32, v + 32);
-        tc::tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 64; ++i) {
-          float x = __uint_as_float(v[i]) * c;
-          if (mask) {
-            const int col = kv0 + 64 * h2 + i;
-            if (col >= kv_len || (CAUSAL && col > row)) x = -INFINITY;
-          }
-          mx = fmaxf(mx, x);
+        for (int i = 0; i < 128; ++i) {
+          const int col = kv0 + i;
+          if (col >= kv_len || (CAUSAL && col > row)) v[i] = masked_bits;
         }
+      }
+      // row maximum of s*c: 8 independent chains
+      float mx;
+      {
+        float m8[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) m8[k] = c >= 0.f ? -INFINITY : INFINITY;
+        if (c >= 0.f) {
+#pragma unroll
+          for (int i = 0; i < 128; ++i) m8[i & 7] = fmaxf(m8[i & 7], __uint_as_float(v[i]));
+          mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+        } else {
+#pragma unroll
+          for (int i = 0; i < 128; ++i) m8[i & 7] = fminf(m8[i & 7], __uint_as_float(v[i]));
+          mx = fminf(fminf(fminf(m8[0], m8[1]), fminf(m8[2], m8[3])), fminf(fminf(m8[4], m8[5]), fminf(m8[6], m8[7])));
+        }
+        mx = (mx == -INFINITY || mx == INFINITY) ? -INFINITY : mx * c;
       }
       bool rescale = false;
       float alpha = 1.f;
@@ -382,7 +404,8 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
         m_ref = mx;
       }
       const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
-      // P smem and O are free once PV(j-1) of this tile has completed
+      // P smem and O are free once PV(j-1) of this tile has completed (O is
+      // rescaled below, after P is written, when this row's reference moved)
       if (j > 0) {
         if (!warp_wait(o_full(t), (j - 1) & 1, abort_flag, a.err)) {
           ok = false;
@@ -390,6 +413,26 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
         }
         tc::fence_after_sync();
       }
+      // P = 2^(s*c - m) in 16 chunks of 8 columns, packed to the K-major
+      // 128B-swizzled P tile; 4 independent partial sums
+      float rs4[4] = {0.f, 0.f, 0.f, 0.f};
+      uint8_t* prow = gb + Lay::kP + t * Lay::kPTile + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+      for (int ch = 0; ch < 16; ++ch) {
+        uint32_t pk[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int i = ch * 8 + 2 * e;
+          const float p0 = ex2(fmaf(__uint_as_float(v[i]), c, -m_use));
+          const float p1 = ex2(fmaf(__uint_as_float(v[i + 1]), c, -m_use));
+          rs4[e] += p0 + p1;
+          pk[e] = pack2<T>(p0, p1);
+        }
+        *reinterpret_cast<uint4*>(prow + (ch >> 3) * (kBM * 128) + (((ch & 7) ^ (r & 7)) << 4)) =
+            make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      }
+      l += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
+      // the S registers are dead now: rescale O (rare, lazy) with the same registers
       if (__any_sync(0xffffffffu, rescale)) {
         const float f = rescale ? alpha : 1.f;
 #pragma unroll
@@ -402,34 +445,6 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
         }
         tc::tmem_wait_st();
       }
-      // pass 2: P = 2^(s*c - m), bf16/fp16 into the K-major 128B-swizzled P tile
-      float rs = 0.f;
-      uint8_t* prow = gb + Lay::kP + t * Lay::kPTile + (r >> 3) * 1024 + (r & 7) * 128;
-#pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
-        tc::tmem_ld32(tl + col_s + 64 * h2, v);
-        tc::tmem_ld32(tl + col_s + 64 * h2 + 32, v + 32);
-        tc::tmem_wait_ld();
-        uint32_t pk[32];
-#pragma unroll
-        for (int i = 0; i < 64; i += 2) {
-          float s0 = __uint_as_float(v[i]), s1 = __uint_as_float(v[i + 1]);
-          float p0 = ex2(fmaf(s0, c, -m_use)), p1 = ex2(fmaf(s1, c, -m_use));
-          if (mask) {
-            const int col = kv0 + 64 * h2 + i;
-            if (col >= kv_len || (CAUSAL && col > row)) p0 = 0.f;
-            if (col + 1 >= kv_len || (CAUSAL && col + 1 > row)) p1 = 0.f;
-          }
-          rs += p0 + p1;
-          pk[i >> 1] = pack2<T>(p0, p1);
-        }
-        uint8_t* sub = prow + h2 * (kBM * 128);
-#pragma unroll
-        for (int ch = 0; ch < 8; ++ch)
-          *reinterpret_cast<uint4*>(sub + ((ch ^ (r & 7)) << 4)) =
-              make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
-      }
-      l += rs;
       fence_proxy_async_smem();
       tc::fence_before_sync();
       mbar_arrive(p_full(t));
