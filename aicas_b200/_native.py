@@ -94,6 +94,7 @@ class RopeAppendParams(ctypes.Structure):
 EXPORTS = {
     "aicas_decode_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(DecodeParams)]),
     "aicas_decode_gqa": (ctypes.c_int, [ctypes.POINTER(DecodeParams), _vp, ctypes.c_size_t, _vp]),
+    "aicas_decode_gqa_noalloc": (ctypes.c_int, [ctypes.POINTER(DecodeParams), _vp]),
     "aicas_merge_partials": (ctypes.c_int, [ctypes.POINTER(MergeParams), _vp]),
     "aicas_prefill_gqa_causal": (ctypes.c_int, [ctypes.POINTER(FmhaParams), _vp]),
     "aicas_varlen_attention": (ctypes.c_int, [ctypes.POINTER(FmhaParams), _vp]),
@@ -121,7 +122,11 @@ def _load() -> ctypes.CDLL:
         raise RuntimeError(_load_error)
     lib = ctypes.CDLL(str(path))
     for name, (res, args) in EXPORTS.items():
-        fn = getattr(lib, name)
+        try:
+            fn = getattr(lib, name)
+        except AttributeError as exc:
+            _load_error = f"native library {path} lacks {name} (stale build?); rebuild with `python -m aicas_b200.build`"
+            raise RuntimeError(_load_error) from exc
         fn.restype = res
         fn.argtypes = args
     _lib = lib

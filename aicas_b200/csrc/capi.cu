@@ -1,6 +1,7 @@
 // C ABI entry points: argument validation, launch planning and error reporting.
 // Nothing here allocates device memory or synchronises the device (except the
 // explicit health query aicas_device_error_flags).
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -197,6 +198,38 @@ int check_fmha(const aicas_fmha_params* p, bool varlen) {
 
 }  // namespace
 
+// Scratch of aicas_decode_gqa_noalloc: split-KV counters (first 1 MiB) and
+// partial results, shared by every call of that entry point on a device.
+// Zero at module load; each completed call leaves its counters at zero and the
+// entry point clears the counters it uses before each launch.
+constexpr size_t kNoAllocScratchBytes = (size_t)8 << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+
+// Device address of g_noalloc_scratch on the current device.  In host code the
+// array's name only stands in for the symbol: the address must be looked up
+// (once per device, with that device current) before a kernel may use it.
+int noalloc_scratch(void** out) {
+  static std::atomic<void*> cached[64];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "aicas_decode_gqa_noalloc: cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(AICAS_ERR_UNSUPPORTED, "aicas_decode_gqa_noalloc: device %d out of range", dev);
+  void* ptr = cached[dev].load();
+  if (ptr == nullptr) {
+    e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess || ptr == nullptr)
+      return cuda_fail(e != cudaSuccess ? e : cudaErrorInvalidSymbol,
+                       "aicas_decode_gqa_noalloc: cudaGetSymbolAddress of the static scratch");
+    cached[dev].store(ptr);
+  }
+  *out = ptr;
+  return AICAS_OK;
+}
+
+}  // namespace
+
 extern "C" {
 
 const char* aicas_version(void) { return "aicas_b200 0.1.0 sm_100a abi 1"; }
@@ -259,6 +292,31 @@ int aicas_decode_gqa(const aicas_decode_params* p, void* workspace, size_t works
                                        static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "decode launch");
   return AICAS_OK;
+}
+
+int aicas_decode_gqa_noalloc(const aicas_decode_params* p, void* stream) {
+  int rc = check_decode(p);
+  if (rc != AICAS_OK) return rc;
+  DecodePlan plan;
+  rc = plan_decode(p, &plan);
+  if (rc != AICAS_OK) return rc;
+  if (plan.ws_bytes > kNoAllocScratchBytes)
+    return fail(AICAS_ERR_UNSUPPORTED,
+                "aicas_decode_gqa_noalloc: this call needs %zu bytes of split-KV scratch but the library's static "
+                "scratch holds %zu; raise split_tokens (fewer splits) or call aicas_decode_gqa with a workspace",
+                plan.ws_bytes, kNoAllocScratchBytes);
+  void* scratch = nullptr;
+  if (plan.ws_bytes > 0) {
+    rc = noalloc_scratch(&scratch);
+    if (rc != AICAS_OK) return rc;
+    // the split counters of this call must start at zero: clear them (a call
+    // that was cut short could have left some behind); partials need no clearing
+    const size_t counter_bytes = (size_t)p->batch * p->num_kv_heads * sizeof(unsigned int);
+    const cudaError_t e = cudaMemsetAsync(static_cast<uint8_t*>(scratch) + plan.ws_count_off, 0, counter_bytes,
+                                          static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "aicas_decode_gqa_noalloc: clearing the split counters");
+  }
+  return aicas_decode_gqa(p, scratch, scratch != nullptr ? kNoAllocScratchBytes : 0, stream);
 }
 
 int aicas_merge_partials(const aicas_merge_params* p, void* stream) {

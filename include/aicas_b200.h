@@ -107,6 +107,22 @@ AICAS_API size_t aicas_decode_workspace_bytes(const aicas_decode_params* p);
 AICAS_API int aicas_decode_gqa(const aicas_decode_params* p, void* workspace, size_t workspace_bytes,
                      void* stream);
 
+/* Same computation as aicas_decode_gqa, for callers that cannot allocate device
+   memory: no counterpart in the reference.  Some hosts hand this library only
+   the pointers of tensors they own and have no way to allocate more (their
+   allocator is not exposed across the C boundary, or their device memory is
+   reserved up front and cudaMalloc is not allowed); this entry point needs no
+   workspace from them.  Its split-KV scratch is one static 8 MiB array inside
+   the library (held by every GPU that loads it, until exit), enough for about
+   7 MiB of partial results (B * Hkv * splits * G * (D + 1) * 4 bytes);
+   larger requests are rejected with AICAS_ERR_UNSUPPORTED (raise split_tokens
+   or use aicas_decode_gqa).  The first call on a device looks up the array's
+   device address and should come before any stream capture on that device.
+   Every call shares the one array and clears the counters it uses on
+   `stream` before launching, so calls that may overlap on the device (other
+   streams, other host threads) race and must be serialised by the caller. */
+AICAS_API int aicas_decode_gqa_noalloc(const aicas_decode_params* p, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Merge P partial (out, LSE) pairs into the final output.                   */
 /* ------------------------------------------------------------------------ */
