@@ -14,7 +14,8 @@
 //   warp 1      TMEM allocator and the single MMA-issuing thread
 //   warps 4-7   softmax + epilogue of query tile 0 (one TMEM lane = one row)
 //   warps 8-11  softmax + epilogue of query tile 1
-// TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [256+D,256+2D).
+// TMEM (512 columns allocated): S0 [0,BN) S1 [BN,2BN) O0 [2BN,2BN+D) O1 [2BN+D,2BN+2D),
+// with BN keys per tile (64 at head_dim 128, 128 at 64).
 // The MMAs are issued in the order S(0,0) S(0,1) | PV(j,0) S(j+1,0) PV(j,1)
 // S(j+1,1) | ..., so while one softmax group works on its S tile the tensor
 // core runs the other tile's products.  The O rescale is lazy: the reference
@@ -36,11 +37,10 @@ namespace aicas {
 namespace {
 
 constexpr int kBM = 128;  // query rows per tile (MMA M)
-constexpr int kBN = 128;  // keys per KV tile
 constexpr int kThreads = 384;
 
 struct FmhaArgs {
-  CUtensorMap tm_q, tm_k, tm_v;  // 4-D, box {64 elements, 128 rows, 1 head, 1 batch}
+  CUtensorMap tm_q, tm_k, tm_v;  // 4-D, box {64 elements, 128 (Q) or BN (K, V) rows, 1 head, 1 batch}
   void* out;
   int64_t o_sb, o_sh, o_ss;
   int q_rows_first, k_rows_first, v_rows_first;  // 1: map dims (D, rows, heads, B); 0: (D, heads, rows, B)
@@ -55,15 +55,28 @@ struct FmhaArgs {
   unsigned int* err;
 };
 
+// 128 keys per KV tile.  One tcgen05.mma (M=128, K=16) costs a fixed issue
+// time that a product with N <= 128 does not cover, so tiles are as wide as the
+// 512 tensor-memory columns allow: at head_dim 128, S0 S1 O0 O1 take all 512
+// columns and P goes through shared memory (an SS P.V product); at head_dim 64
+// P fits in tensor memory next to S and O (a TS P.V product: A from tensor
+// memory), which also frees the shared memory the P tiles would take.
+//   S_t at t*128 (fp32);  head_dim 128: O_t at 256 + t*128;
+//   head_dim 64: P_t at 256 + t*64 (16-bit pairs), O_t at 384 + t*64.
 template <int D>
 struct Layout {
+  static constexpr int kBN = 128;
+  static constexpr bool kPTmem = D == 64;
   static constexpr uint32_t kQTile = kBM * D * 2;
   static constexpr uint32_t kKVTile = kBN * D * 2;
-  static constexpr uint32_t kPTile = kBM * kBN * 2;
-  static constexpr int kStages = D == 128 ? 3 : 8;
+  static constexpr uint32_t kPTile = kPTmem ? 0 : kBM * kBN * 2;
+  static constexpr uint32_t kColP = 2 * kBN;
+  static constexpr uint32_t kColO = kPTmem ? 3 * kBN : 2 * kBN;
+  static_assert(kColO + 2 * D <= 512, "tensor memory budget");
   static constexpr uint32_t kQ = 0;
   static constexpr uint32_t kP = kQ + 2 * kQTile;
   static constexpr uint32_t kKV = kP + 2 * kPTile;
+  static constexpr int kStages = kPTmem ? 10 : 3;
   static constexpr uint32_t kBar = kKV + kStages * kKVTile;
   static constexpr int kNumBars = 1 + 2 * kStages + 8 + 1;
   static constexpr uint32_t kMisc = kBar + kNumBars * 8;  // [tmem base][abort][schedule x 8]
@@ -71,10 +84,73 @@ struct Layout {
   static_assert(kBytes <= 232448, "shared memory budget");
 };
 
+// Position in the K/V load sequence K0, K1, V0, K2, V1, ..., V(n-1): keys run
+// one tile ahead of values, so each ring stage is refilled by the tile whose
+// previous occupant is released earliest (a K tile is free after both S
+// products of its iteration, a V tile only after both P.V products).
+__host__ __device__ __forceinline__ int kv_load_index_k(int m) { return m == 0 ? 0 : 2 * m - 1; }
+__host__ __device__ __forceinline__ int kv_load_index_v(int j, int n) { return min(2 * j + 2, 2 * n - 1); }
+
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// ---- packed fp32 pairs (sm_100 f32x2 instructions: two lanes of work per issue)
+__device__ __forceinline__ uint64_t f2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void unf2(uint64_t r, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(r));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ float fmin3(float a, float b, float c) {
+  float d;
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x for a pair on the FMA pipe, to take part of the exponentials off the
+// MUFU unit (which alone would bound the softmax).  x = n + f with n the
+// nearest integer (added to the exponent field) and f in [-1/2, 1/2]; 2^f by
+// a cubic fitted here for minimal relative error (max 8.4e-5, far below the
+// bf16/fp16 rounding P gets next).  x is clamped at -125 so the exponent stays
+// normal; callers use it only on tiles without masked (-inf) entries.
+__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x2) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23: x + kRound rounds x to an integer in the mantissa
+  constexpr float kC0 = 9.999196109e-01f, kC1 = 6.932621430e-01f, kC2 = 2.427139391e-01f, kC3 = 5.521300572e-02f;
+  float x0, x1;
+  unf2(x2, x0, x1);
+  const uint64_t x = f2(fmaxf(x0, -125.f), fmaxf(x1, -125.f));
+  const uint64_t t = fadd2(x, f2(kRound, kRound));
+  const uint64_t n = fadd2(t, f2(-kRound, -kRound));
+  const uint64_t fr = ffma2(n, f2(-1.f, -1.f), x);
+  uint64_t q = ffma2(f2(kC3, kC3), fr, f2(kC2, kC2));
+  q = ffma2(q, fr, f2(kC1, kC1));
+  q = ffma2(q, fr, f2(kC0, kC0));
+  float q0, q1, t0, t1;
+  unf2(q, q0, q1);
+  unf2(t, t0, t1);
+  // the low mantissa bits of t hold n; shifted to the exponent field they add n
+  return f2(__int_as_float(__float_as_int(q0) + (__float_as_int(t0) << 23)),
+            __int_as_float(__float_as_int(q1) + (__float_as_int(t1) << 23)));
 }
 
 template <typename T>
@@ -104,7 +180,11 @@ template <typename T, int D, bool CAUSAL, bool VARLEN>
 __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_constant__ FmhaArgs a) {
   using Lay = Layout<D>;
   constexpr int NS = Lay::kStages;
+  constexpr int kBN = Lay::kBN;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+  // pairs out of every 8 (16 columns) whose exponential runs on the FMA pipe:
+  // about 1/4 at head_dim 128, 3/8 at 64 where the products are shorter
+  constexpr int kPolyPairs = D == 128 ? 2 : 3;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t sb = (raw + 1023u) & ~1023u;
@@ -251,10 +331,21 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
                    q_base + (t ? row1 : row0), t ? head1 : head0, b, q_full);
       int issued = 0;
       for (int idx = 0; idx < 2 * n_kv; ++idx) {
+        // idx -> tile: 0 is K0, then K(j+1), V(j) pairs, the last V alone
+        bool is_v;
+        int j;
+        if (idx == 0) {
+          is_v = false;
+          j = 0;
+        } else if (idx == 2 * n_kv - 1) {
+          is_v = true;
+          j = n_kv - 1;
+        } else {
+          is_v = (idx & 1) == 0;
+          j = is_v ? (idx - 2) / 2 : (idx + 1) / 2;
+        }
         const int s = idx % NS, u = idx / NS;
         if (u > 0 && !mbar_wait(kv_empty(s), (u - 1) & 1, abort_flag, a.err)) break;
-        const bool is_v = idx & 1;
-        const int j = idx >> 1;
         mbar_arrive_expect_tx(kv_full(s), Lay::kKVTile);
         for (int bx = 0; bx < D / 64; ++bx)
           tma_tile(sb + Lay::kKV + s * Lay::kKVTile + bx * (kBN * 128), is_v ? &a.tm_v : &a.tm_k,
@@ -272,22 +363,39 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
     if (lane == 0) {
       constexpr uint32_t kIdS = tc::idesc_f16(kBF16, kBM, kBN, false, false);
       constexpr uint32_t kIdPV = tc::idesc_f16(kBF16, kBM, D, false, true);
+      // Descriptors are built once.  A descriptor depends on its tile's address
+      // only through the 14-bit start-address field (address >> 4, below 2^14
+      // for every shared-memory address here), so moving to another tile or
+      // k-step is one 64-bit add of a constant: the issuing thread spends its
+      // time issuing products, not rebuilding descriptors.
+      const uint64_t dq0 = tc::smem_desc_sw128(sb + Lay::kQ, 16, 1024);
+      const uint64_t dk0 = tc::smem_desc_sw128(sb + Lay::kKV, 16, 1024);
+      const uint64_t dv0 = tc::smem_desc_sw128(sb + Lay::kKV, kBN * 128, 1024);
       auto issue_s = [&](int stage, int t) {
+        const uint64_t qa = dq0 + ((uint64_t)(t * Lay::kQTile) >> 4);
+        const uint64_t kb = dk0 + ((uint64_t)(stage * Lay::kKVTile) >> 4);
+        const uint32_t dst = tmem + t * kBN;
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t aa = sb + Lay::kQ + t * Lay::kQTile + (kk >> 2) * (kBM * 128) + (kk & 3) * 32;
-          const uint32_t bb = sb + Lay::kKV + stage * Lay::kKVTile + (kk >> 2) * (kBN * 128) + (kk & 3) * 32;
-          tc::mma_f16_ss(tmem + t * 128, tc::smem_desc_sw128(aa, 16, 1024), tc::smem_desc_sw128(bb, 16, 1024), kIdS,
-                         kk > 0);
-        }
+        for (int kk = 0; kk < D / 16; ++kk)
+          tc::mma_f16_ss(dst, qa + (uint64_t)(((kk >> 2) * (kBM * 128) + (kk & 3) * 32) >> 4),
+                         kb + (uint64_t)(((kk >> 2) * (kBN * 128) + (kk & 3) * 32) >> 4), kIdS, kk > 0 ? 1u : 0u);
       };
+      const uint64_t dp0 = tc::smem_desc_sw128(sb + Lay::kP, 16, 1024);
       auto issue_pv = [&](int j, int stage, int t) {
+        const uint64_t vb = dv0 + ((uint64_t)(stage * Lay::kKVTile) >> 4);
+        const uint32_t dst = tmem + Lay::kColO + t * D;
+        if constexpr (Lay::kPTmem) {
+          const uint32_t pa = tmem + Lay::kColP + t * (kBN / 2);
 #pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
-          const uint32_t aa = sb + Lay::kP + t * Lay::kPTile + (kk >> 2) * (kBM * 128) + (kk & 3) * 32;
-          const uint32_t bb = sb + Lay::kKV + stage * Lay::kKVTile + kk * (16 * 128);
-          tc::mma_f16_ss(tmem + 256 + t * D, tc::smem_desc_sw128(aa, 16, 1024),
-                         tc::smem_desc_sw128(bb, kBN * 128, 1024), kIdPV, (j > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < kBN / 16; ++kk)
+            tc::mma_f16_ts(dst, pa + kk * 8, vb + (uint64_t)((kk * (16 * 128)) >> 4), kIdPV,
+                           (j > 0 || kk > 0) ? 1u : 0u);
+        } else {
+          const uint64_t pa = dp0 + ((uint64_t)(t * Lay::kPTile) >> 4);
+#pragma unroll
+          for (int kk = 0; kk < kBN / 16; ++kk)
+            tc::mma_f16_ss(dst, pa + (uint64_t)(((kk >> 2) * (kBM * 128) + (kk & 3) * 32) >> 4),
+                           vb + (uint64_t)((kk * (16 * 128)) >> 4), kIdPV, (j > 0 || kk > 0) ? 1u : 0u);
         }
       };
       bool ok = !*abort_flag && mbar_wait(q_full, 0, abort_flag, a.err);
@@ -301,13 +409,13 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
           tc::commit(s_full(1));
           tc::commit(kv_empty(0));
         }
-        // Steady state, in the order the softmax groups release their inputs:
-        // S(j+1,0) as soon as group 0 has READ S(j,0) (not after its softmax),
-        // PV(j,0) once P(j,0) is written, then the same for tile 1.
         for (int j = 0; ok && j < n_kv; ++j) {
-          const int iv = 2 * j + 1, ik = 2 * j + 2;
+          const int iv = kv_load_index_v(j, n_kv), ik = kv_load_index_k(j + 1);
           const int sv = iv % NS, sk = ik % NS;
           const bool more = j + 1 < n_kv;
+          // Per-tile order, as the softmax groups release their inputs:
+          // S(j+1,0) as soon as group 0 has READ S(j,0) (not after its softmax),
+          // PV(j,0) once P(j,0) is written, then the same for tile 1.
           if (more) {
             ok = mbar_wait(kv_full(sk), (ik / NS) & 1, abort_flag, a.err) &&
                  mbar_wait(s_free(0), j & 1, abort_flag, a.err);
@@ -351,11 +459,12 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
     const int row = tile_row0 + r;
     const bool row_valid = row < q_len;
     const uint32_t tl = tmem + ((uint32_t)(qw * 32) << 16);
-    const uint32_t col_s = t * 128, col_o = 256 + t * D;
+    const uint32_t col_s = t * kBN, col_p = Lay::kColP + t * (kBN / 2), col_o = Lay::kColO + t * D;
+    uint8_t* prow = gb + Lay::kP + t * Lay::kPTile + (r >> 3) * 1024 + (r & 7) * 128;  // P row (head_dim 128)
     const float c = a.scale_log2;
     float m_ref = -INFINITY, l = 0.f;
     bool ok = !*abort_flag;
-    uint32_t v[128];  // the S row of this thread, then reused for O chunks
+    uint32_t v[kBN];  // the S row of this thread, then reused for O chunks
     const uint32_t masked_bits = __float_as_uint(c >= 0.f ? -INFINITY : INFINITY);  // s*c -> -inf
     for (int j = 0; ok && j < n_kv; ++j) {
       if (!warp_wait(s_full(t), j & 1, abort_flag, a.err)) {
@@ -364,7 +473,7 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
       }
       tc::fence_after_sync();
 #pragma unroll
-      for (int cc = 0; cc < 4; ++cc) tc::tmem_ld32(tl + col_s + 32 * cc, v + 32 * cc);
+      for (int cc = 0; cc < kBN / 32; ++cc) tc::tmem_ld32(tl + col_s + 32 * cc, v + 32 * cc);
       tc::tmem_wait_ld();
       // S(j) is in registers: the tensor core may overwrite it with S(j+1) now
       tc::fence_before_sync();
@@ -373,25 +482,29 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
       const bool mask = (kv0 + kBN > kv_len) || (CAUSAL && kv0 + kBN - 1 > tile_row0);
       if (mask) {
 #pragma unroll
-        for (int i = 0; i < 128; ++i) {
+        for (int i = 0; i < kBN; ++i) {
           const int col = kv0 + i;
           if (col >= kv_len || (CAUSAL && col > row)) v[i] = masked_bits;
         }
       }
-      // row maximum of s*c: 8 independent chains
+      // row maximum of s*c: 4 independent chains of 3-input max
       float mx;
       {
-        float m8[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) m8[k] = c >= 0.f ? -INFINITY : INFINITY;
+        float m4[4];
         if (c >= 0.f) {
 #pragma unroll
-          for (int i = 0; i < 128; ++i) m8[i & 7] = fmaxf(m8[i & 7], __uint_as_float(v[i]));
-          mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+          for (int k = 0; k < 4; ++k) m4[k] = -INFINITY;
+#pragma unroll
+          for (int i = 0; i < kBN; i += 2)
+            m4[(i >> 1) & 3] = fmax3(m4[(i >> 1) & 3], __uint_as_float(v[i]), __uint_as_float(v[i + 1]));
+          mx = fmax3(m4[0], m4[1], fmaxf(m4[2], m4[3]));
         } else {
 #pragma unroll
-          for (int i = 0; i < 128; ++i) m8[i & 7] = fminf(m8[i & 7], __uint_as_float(v[i]));
-          mx = fminf(fminf(fminf(m8[0], m8[1]), fminf(m8[2], m8[3])), fminf(fminf(m8[4], m8[5]), fminf(m8[6], m8[7])));
+          for (int k = 0; k < 4; ++k) m4[k] = INFINITY;
+#pragma unroll
+          for (int i = 0; i < kBN; i += 2)
+            m4[(i >> 1) & 3] = fmin3(m4[(i >> 1) & 3], __uint_as_float(v[i]), __uint_as_float(v[i + 1]));
+          mx = fmin3(m4[0], m4[1], fminf(m4[2], m4[3]));
         }
         mx = (mx == -INFINITY || mx == INFINITY) ? -INFINITY : mx * c;
       }
@@ -404,8 +517,8 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
         m_ref = mx;
       }
       const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
-      // P smem and O are free once PV(j-1) of this tile has completed (O is
-      // rescaled below, after P is written, when this row's reference moved)
+      // the P columns and O are free once PV(j-1) of this tile has completed (O
+      // is rescaled below, after P is written, when this row's reference moved)
       if (j > 0) {
         if (!warp_wait(o_full(t), (j - 1) & 1, abort_flag, a.err)) {
           ok = false;
@@ -413,24 +526,58 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
         }
         tc::fence_after_sync();
       }
-      // P = 2^(s*c - m) in 16 chunks of 8 columns, packed to the K-major
-      // 128B-swizzled P tile; 4 independent partial sums
-      float rs4[4] = {0.f, 0.f, 0.f, 0.f};
-      uint8_t* prow = gb + Lay::kP + t * Lay::kPTile + (r >> 3) * 1024 + (r & 7) * 128;
+      // P = 2^(s*c - m), packed to 16-bit pairs and stored 64 keys at a time to
+      // this row's lane of the P columns (head_dim 64) or its smem row (128).  Pairs
+      // are scaled with one f32x2 FMA; on tiles without masked entries
+      // kPolyPairs of every 8 pairs take the polynomial exponential, the rest
+      // ex2.approx; partial sums in f32x2 accumulators.
+      uint64_t rs2[2] = {f2(0.f, 0.f), f2(0.f, 0.f)};
+      const uint64_t c2 = f2(c, c), nm2 = f2(-m_use, -m_use);
 #pragma unroll
-      for (int ch = 0; ch < 16; ++ch) {
-        uint32_t pk[4];
+      for (int h = 0; h < kBN / 64; ++h) {
+        uint32_t pk[32];
+        if (mask) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int i = ch * 8 + 2 * e;
-          const float p0 = ex2(fmaf(__uint_as_float(v[i]), c, -m_use));
-          const float p1 = ex2(fmaf(__uint_as_float(v[i + 1]), c, -m_use));
-          rs4[e] += p0 + p1;
-          pk[e] = pack2<T>(p0, p1);
+          for (int e = 0; e < 32; ++e) {
+            const int i = 64 * h + 2 * e;
+            float x0, x1;
+            unf2(ffma2(f2(__uint_as_float(v[i]), __uint_as_float(v[i + 1])), c2, nm2), x0, x1);
+            const float p0 = ex2(x0), p1 = ex2(x1);
+            rs2[e & 1] = fadd2(rs2[e & 1], f2(p0, p1));
+            pk[e] = pack2<T>(p0, p1);
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int i = 64 * h + 2 * e;
+            const uint64_t x2 = ffma2(f2(__uint_as_float(v[i]), __uint_as_float(v[i + 1])), c2, nm2);
+            float p0, p1;
+            if ((e & 7) < kPolyPairs) {
+              unf2(exp2_poly2(x2), p0, p1);
+            } else {
+              float x0, x1;
+              unf2(x2, x0, x1);
+              p0 = ex2(x0);
+              p1 = ex2(x1);
+            }
+            rs2[e & 1] = fadd2(rs2[e & 1], f2(p0, p1));
+            pk[e] = pack2<T>(p0, p1);
+          }
         }
-        *reinterpret_cast<uint4*>(prow + (ch >> 3) * (kBM * 128) + (((ch & 7) ^ (r & 7)) << 4)) =
-            make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        if constexpr (Lay::kPTmem) {
+          tc::tmem_st32(tl + col_p + 32 * h, pk);
+        } else {
+          // K-major 128B-swizzled P tile: 16-byte chunk c of row r at c ^ (r % 8)
+          uint8_t* sub = prow + h * (kBM * 128);
+#pragma unroll
+          for (int ch = 0; ch < 8; ++ch)
+            *reinterpret_cast<uint4*>(sub + ((ch ^ (r & 7)) << 4)) =
+                make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
+        }
       }
+      float rs4[4];
+      unf2(rs2[0], rs4[0], rs4[1]);
+      unf2(rs2[1], rs4[2], rs4[3]);
       l += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
       // the S registers are dead now: rescale O (rare, lazy) with the same registers
       if (__any_sync(0xffffffffu, rescale)) {
@@ -445,11 +592,12 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
         }
         tc::tmem_wait_st();
       }
-      fence_proxy_async_smem();
+      if constexpr (Lay::kPTmem) tc::tmem_wait_st();  // P is in tensor memory before PV(j) may read it
+      else fence_proxy_async_smem();                   // P in shared memory is visible to the tensor core
       tc::fence_before_sync();
       mbar_arrive(p_full(t));
     }
-    // epilogue: O / l -> global, one row per thread
+    // epilogue: O / l -> global
     T* orow = static_cast<T*>(a.out) + (int64_t)b * a.o_sb + (int64_t)(t ? head1 : head0) * a.o_sh +
               (int64_t)(q_base + row) * a.o_ss;
     if (ok && n_kv > 0) {
@@ -510,7 +658,7 @@ EncodeTiledFn encode_fn() {
 // 4-D map over [B, heads, rows, D] (element strides), the two middle dimensions
 // ordered by increasing stride as the tensor-map encoder expects.
 bool make_map(CUtensorMap* m, const void* ptr, bool bf16, int d, int rows, int heads, int batch, int64_t s_b,
-              int64_t s_h, int64_t s_s, int* rows_first, char* err, size_t errlen) {
+              int64_t s_h, int64_t s_s, int box_rows, int* rows_first, char* err, size_t errlen) {
   EncodeTiledFn enc = encode_fn();
   if (enc == nullptr) {
     snprintf(err, errlen, "cuTensorMapEncodeTiled is unavailable from the driver");
@@ -527,9 +675,9 @@ bool make_map(CUtensorMap* m, const void* ptr, bool bf16, int d, int rows, int h
   dims[0] = (cuuint64_t)d;
   box[0] = 64;
   if (rf) {
-    dims[1] = rows; dims[2] = heads; strides[0] = s_s * 2; strides[1] = s_h * 2; box[1] = 128; box[2] = 1;
+    dims[1] = rows; dims[2] = heads; strides[0] = s_s * 2; strides[1] = s_h * 2; box[1] = box_rows; box[2] = 1;
   } else {
-    dims[1] = heads; dims[2] = rows; strides[0] = s_h * 2; strides[1] = s_s * 2; box[1] = 1; box[2] = 128;
+    dims[1] = heads; dims[2] = rows; strides[0] = s_h * 2; strides[1] = s_s * 2; box[1] = 1; box[2] = box_rows;
   }
   dims[3] = batch;
   strides[2] = s_b * 2;
@@ -578,12 +726,13 @@ int run_fmha(const aicas_fmha_params* p, bool varlen, cudaStream_t stream, unsig
   const bool bf16 = p->dtype == AICAS_DTYPE_BF16;
   FmhaArgs a;
   memset(&a, 0, sizeof(a));
+  const int kv_box = Layout<128>::kBN;
   if (!make_map(&a.tm_q, p->q, bf16, p->head_dim, p->seq_len_q, p->num_q_heads, p->batch, p->q_stride_b,
-                p->q_stride_h, p->q_stride_s, &a.q_rows_first, err, errlen) ||
+                p->q_stride_h, p->q_stride_s, kBM, &a.q_rows_first, err, errlen) ||
       !make_map(&a.tm_k, p->k, bf16, p->head_dim, p->seq_len_kv, p->num_kv_heads, p->batch, p->k_stride_b,
-                p->k_stride_h, p->k_stride_s, &a.k_rows_first, err, errlen) ||
+                p->k_stride_h, p->k_stride_s, kv_box, &a.k_rows_first, err, errlen) ||
       !make_map(&a.tm_v, p->v, bf16, p->head_dim, p->seq_len_kv, p->num_kv_heads, p->batch, p->v_stride_b,
-                p->v_stride_h, p->v_stride_s, &a.v_rows_first, err, errlen))
+                p->v_stride_h, p->v_stride_s, kv_box, &a.v_rows_first, err, errlen))
     return AICAS_ERR_UNSUPPORTED;
   a.out = p->out;
   a.o_sb = p->o_stride_b;
