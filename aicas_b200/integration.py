@@ -1,0 +1,268 @@
+"""End-to-end integration check: greedy generation on a random-init model with
+Qwen3-VL-2B's architecture, switched to this backend by
+:func:`install_qwen3vl_triton_attention`, against the same weights on
+PyTorch SDPA attention.
+
+The check follows the organiser harness of the reference project
+(evaluation_wrapper.py:40-66 loads the model, :380-405 installs the attention
+patch, :505-516 runs ``model.generate`` greedily with the KV cache on), with
+three differences forced by an offline box: the weights are random (seeded),
+the prompt is synthetic (a text span, one image of ``grid_hw`` patches between
+the vision start/end tokens, more text; the mixed image+text prompt of the
+causal-prefill workload), and the pixels are seeded noise.  The architecture
+numbers below are those of the public Qwen3-VL-2B-Instruct configuration; the
+attention shapes they give are the ones the kernels are built and measured on
+(text: 16 query heads over 8 KV heads at head_dim 128; vision: 16 heads at 64).
+
+What is compared (the tolerances live in the tests that call these helpers):
+  * ``token_match``: the fraction of generated positions where the patched and
+    the SDPA greedy sequences agree, counted up to their first divergence;
+  * ``max_logit_gap``: the patched tokens fed back, teacher-forced, through
+    the SDPA model: at every generated position, SDPA's best logit minus its
+    logit for the patched token (0 where SDPA would pick the same token).  On
+    a random-init model the top logits sit close together, so a divergence
+    after a near-tie is expected; a large gap would mean the patched model
+    chose a token SDPA rates as clearly worse.
+"""
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass
+
+import torch
+
+from .backends import TEXT_BACKEND_KEY, VISION_BACKEND_KEY
+from .patch import install_qwen3vl_triton_attention
+
+# Qwen3-VL-2B-Instruct: language model and vision tower hyper-parameters.
+QWEN3VL_2B_TEXT = dict(
+    hidden_size=2048,
+    intermediate_size=6144,
+    num_hidden_layers=28,
+    num_attention_heads=16,
+    num_key_value_heads=8,
+    head_dim=128,
+    vocab_size=151936,
+    max_position_embeddings=262144,
+    rms_norm_eps=1e-6,
+    rope_theta=5000000.0,
+    rope_scaling={"rope_type": "default", "mrope_section": [24, 20, 20], "mrope_interleaved": True},
+    tie_word_embeddings=True,
+)
+QWEN3VL_2B_VISION = dict(
+    depth=24,
+    hidden_size=1024,
+    intermediate_size=4096,
+    num_heads=16,
+    out_hidden_size=2048,
+    patch_size=16,
+    spatial_merge_size=2,
+    temporal_patch_size=2,
+    in_channels=3,
+    num_position_embeddings=2304,
+    deepstack_visual_indexes=[5, 11, 17],
+    hidden_act="gelu_pytorch_tanh",
+)
+IMAGE_TOKEN_ID = 151655
+VIDEO_TOKEN_ID = 151656
+VISION_START_TOKEN_ID = 151652
+VISION_END_TOKEN_ID = 151653
+
+
+def qwen3vl_config(text: dict | None = None, vision: dict | None = None):
+    """A ``Qwen3VLConfig`` with the 2B architecture, fields overridable (the
+    CPU tests shrink it)."""
+    from transformers import Qwen3VLConfig
+
+    t = dict(QWEN3VL_2B_TEXT, **(text or {}))
+    v = dict(QWEN3VL_2B_VISION, **(vision or {}))
+    cfg = Qwen3VLConfig(
+        text_config=t,
+        vision_config=v,
+        image_token_id=IMAGE_TOKEN_ID,
+        video_token_id=VIDEO_TOKEN_ID,
+        vision_start_token_id=VISION_START_TOKEN_ID,
+        vision_end_token_id=VISION_END_TOKEN_ID,
+        tie_word_embeddings=t["tie_word_embeddings"],
+    )
+    return cfg
+
+
+def build_random_model(config, dtype: torch.dtype, device: torch.device | str, seed: int = 0):
+    """Random-init ``Qwen3VLForConditionalGeneration`` on ``device`` (weights
+    drawn by the model's own initialiser from ``seed``), in eval mode, on SDPA."""
+    from transformers import Qwen3VLForConditionalGeneration
+
+    config._attn_implementation = "sdpa"
+    torch.manual_seed(seed)
+    with torch.device(device):
+        model = Qwen3VLForConditionalGeneration(config)
+    model = model.to(dtype).eval()
+    set_attention(model, "sdpa")
+    return model
+
+
+def set_attention(model, which: str) -> None:
+    """Point the four config objects the patch entry point mutates at
+    ``which``: "sdpa" for the unpatched baseline, "aicas" for this backend
+    (through :func:`install_qwen3vl_triton_attention`)."""
+    if which == "aicas":
+        state = install_qwen3vl_triton_attention(model)
+        if not state["triton_available"]:
+            raise RuntimeError("the aicas_b200 native library is not loadable; the patched model cannot run")
+        return
+    if which != "sdpa":
+        raise ValueError(f"unknown attention implementation {which!r}")
+    base = getattr(model, "model", None)
+    for cfg in (
+        getattr(getattr(base, "visual", None), "config", None),
+        getattr(getattr(base, "language_model", None), "config", None),
+        getattr(model.config, "vision_config", None),
+        getattr(model.config, "text_config", None),
+    ):
+        if cfg is not None:
+            cfg._attn_implementation = "sdpa"
+
+
+def attention_in_use(model) -> tuple[str, str]:
+    """(vision, text) attention implementations the model will call."""
+    return model.config.vision_config._attn_implementation, model.config.text_config._attn_implementation
+
+
+def synthetic_prompt(config, batch: int, seq_len: int, grid_hw: tuple[int, int] = (64, 100), text_before: int = 100,
+                     seed: int = 0, dtype: torch.dtype = torch.bfloat16, device: torch.device | str = "cpu") -> dict:
+    """Model inputs for ``batch`` prompts of exactly ``seq_len`` tokens, each
+    ``text_before`` text tokens, <vision_start>, the image tokens of one
+    ``grid_hw`` patch grid (grid_h * grid_w / merge^2 of them), <vision_end>,
+    then text to fill the length.  Text ids are drawn below the special-token
+    range; pixels are N(0, 1) patches as the image processor would flatten
+    them (channels x temporal x patch x patch per row)."""
+    vc = config.vision_config
+    gh, gw = grid_hw
+    merge = vc.spatial_merge_size
+    if gh % merge or gw % merge:
+        raise ValueError("the patch grid must be divisible by the spatial merge size")
+    n_img = gh * gw // (merge * merge)
+    n_after = seq_len - text_before - n_img - 2
+    if n_after < 0:
+        raise ValueError(f"seq_len {seq_len} cannot hold {text_before} text + {n_img} image tokens")
+    g = torch.Generator().manual_seed(seed)
+    text_vocab = min(config.text_config.vocab_size, VISION_START_TOKEN_ID)
+    ids = torch.randint(0, text_vocab, (batch, seq_len), generator=g, dtype=torch.long)
+    ids[:, text_before] = VISION_START_TOKEN_ID
+    ids[:, text_before + 1:text_before + 1 + n_img] = IMAGE_TOKEN_ID
+    ids[:, text_before + 1 + n_img] = VISION_END_TOKEN_ID
+    mm = torch.zeros(batch, seq_len, dtype=torch.int32)
+    mm[:, text_before + 1:text_before + 1 + n_img] = 1
+    row = vc.in_channels * vc.temporal_patch_size * vc.patch_size * vc.patch_size
+    pixels = torch.randn(batch * gh * gw, row, generator=g).to(dtype)
+    thw = torch.tensor([[1, gh, gw]] * batch, dtype=torch.long)
+    return {
+        "input_ids": ids.to(device),
+        "attention_mask": torch.ones(batch, seq_len, dtype=torch.long, device=device),
+        "mm_token_type_ids": mm.to(device),
+        "pixel_values": pixels.to(device),
+        "image_grid_thw": thw.to(device),
+    }
+
+
+@dataclass
+class GenerateRun:
+    tokens: torch.Tensor  # [B, new] generated ids
+    seconds: float  # whole generate() call, device-synchronised
+    ttft_seconds: float  # generate() of one new token (prefill + first sample)
+
+    @property
+    def tokens_per_s(self) -> float:
+        return self.tokens.numel() / self.seconds if self.seconds > 0 else float("nan")
+
+
+def _sync(device) -> None:
+    if torch.device(device).type == "cuda":
+        torch.cuda.synchronize(device)
+
+
+@torch.no_grad()
+def greedy_generate(model, inputs: dict, max_new_tokens: int, timed: bool = True) -> GenerateRun:
+    """``model.generate`` as the organiser harness calls it (greedy, KV cache
+    on, evaluation_wrapper.py:509-516), timed on the host around
+    device-synchronised calls.  TTFT is a separate one-token generate."""
+    kw = dict(do_sample=False, use_cache=True, pad_token_id=0)
+    device = inputs["input_ids"].device
+    ttft = float("nan")
+    if timed:
+        _sync(device)
+        t0 = time.perf_counter()
+        model.generate(**inputs, max_new_tokens=1, min_new_tokens=1, **kw)
+        _sync(device)
+        ttft = time.perf_counter() - t0
+    _sync(device)
+    t0 = time.perf_counter()
+    out = model.generate(**inputs, max_new_tokens=max_new_tokens, min_new_tokens=max_new_tokens, **kw)
+    _sync(device)
+    dt = time.perf_counter() - t0
+    return GenerateRun(tokens=out[:, inputs["input_ids"].shape[1]:], seconds=dt, ttft_seconds=ttft)
+
+
+def token_match(a: torch.Tensor, b: torch.Tensor) -> float:
+    """Fraction of positions (over the batch) before each row's first
+    disagreement."""
+    n = min(a.shape[1], b.shape[1])
+    same = (a[:, :n] == b[:, :n]).to(torch.int32)
+    prefix = torch.cumprod(same, dim=1).sum(dim=1)
+    return float(prefix.sum()) / float(a.shape[0] * n) if n else 1.0
+
+
+@torch.no_grad()
+def teacher_forced_gap(model, inputs: dict, tokens: torch.Tensor) -> torch.Tensor:
+    """[B, new] gaps: the model's best logit minus its logit for ``tokens``, at
+    each generated position, with ``tokens`` fed back as the continuation."""
+    ids = torch.cat([inputs["input_ids"], tokens], dim=1)
+    n_new = tokens.shape[1]
+    full = dict(inputs)
+    full["input_ids"] = ids
+    full["attention_mask"] = torch.ones_like(ids)
+    mm = inputs["mm_token_type_ids"]
+    full["mm_token_type_ids"] = torch.cat([mm, torch.zeros(mm.shape[0], n_new, dtype=mm.dtype, device=mm.device)], 1)
+    model.model.rope_deltas = None
+    logits = model(**full, use_cache=False, logits_to_keep=n_new + 1).logits.float()
+    pred = logits[:, :-1]  # position i predicts generated token i
+    best = pred.max(dim=-1).values
+    chosen = pred.gather(-1, tokens.unsqueeze(-1)).squeeze(-1)
+    return best - chosen
+
+
+def run_check(batch: int = 8, seq_len: int = 2048, max_new_tokens: int = 128, grid_hw=(64, 100),
+              dtype: torch.dtype = torch.bfloat16, device: str | torch.device = "cuda:0", seed: int = 0,
+              text: dict | None = None, vision: dict | None = None, timed: bool = True) -> dict:
+    """Build the model, generate greedily with SDPA and with this backend, and
+    compare.  Returns the numbers the integration test and the benchmark
+    report."""
+    config = qwen3vl_config(text, vision)
+    model = build_random_model(config, dtype, device, seed)
+    inputs = synthetic_prompt(config, batch, seq_len, grid_hw, seed=seed, dtype=dtype, device=device)
+    # warm-up of both paths (allocator, library load, tensor-map encoder)
+    warm = {k: (v[:1] if k != "pixel_values" else v[: v.shape[0] // batch]) for k, v in inputs.items()}
+    set_attention(model, "sdpa")
+    greedy_generate(model, warm, 2, timed=False)
+    ref = greedy_generate(model, inputs, max_new_tokens, timed)
+    set_attention(model, "aicas")
+    assert attention_in_use(model) == (VISION_BACKEND_KEY, TEXT_BACKEND_KEY)
+    greedy_generate(model, warm, 2, timed=False)
+    ours = greedy_generate(model, inputs, max_new_tokens, timed)
+    set_attention(model, "sdpa")
+    gap = teacher_forced_gap(model, inputs, ours.tokens)
+    result = {
+        "batch": batch,
+        "prompt_tokens": seq_len,
+        "new_tokens": max_new_tokens,
+        "image_grid": list(grid_hw),
+        "dtype": str(dtype).replace("torch.", ""),
+        "token_match": token_match(ours.tokens, ref.tokens),
+        "max_logit_gap": float(gap.max()),
+        "mean_logit_gap": float(gap.mean()),
+        "patched": {"tokens_per_s": ours.tokens_per_s, "seconds": ours.seconds, "ttft_s": ours.ttft_seconds},
+        "sdpa": {"tokens_per_s": ref.tokens_per_s, "seconds": ref.seconds, "ttft_s": ref.ttft_seconds},
+    }
+    del model
+    return result

@@ -437,6 +437,20 @@ def time_varlen(args, world, device, peaks) -> dict:
 # ------------------------------------------------------------------ CPU (reference) path
 
 
+def run_generate(device) -> dict:
+    """Configuration 4's end-to-end check: greedy generate of 128 tokens after
+    a 2048-token image+text prompt, batch 8, on a random-init model with the
+    Qwen3-VL-2B architecture, patched against SDPA on the same weights (host
+    timed around device-synchronised generate calls; not a roofline)."""
+    from aicas_b200 import integration
+
+    r = integration.run_check(batch=8, seq_len=2048, max_new_tokens=128, grid_hw=(64, 100), device=device)
+    r["workload"] = "cfg4-e2e: random-init Qwen3-VL-2B-shaped model, 8 prompts x 2048 tokens (1600 image), greedy 128"
+    r["speedup_vs_sdpa"] = r["patched"]["tokens_per_s"] / r["sdpa"]["tokens_per_s"]
+    torch.cuda.empty_cache()
+    return r
+
+
 def cpu_decode_sample(target_s: float, max_layers: int = 100000) -> dict:
     """Times the reference's CPU path (oracle/reference_cpu.py) on whole config-2
     layers (all 64 requests) on the host cores; returns GB/s of the same metric."""
@@ -508,7 +522,9 @@ def main(argv=None) -> int:
                     help="skip the tensor-core prefill / ViT measurements")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     ap.add_argument("--no-e2e", dest="e2e", action="store_false", help="skip the end-to-end host-buffer measurement")
-    ap.add_argument("--only", choices=["decode", "split_kv", "prefill", "vit"], default=None,
+    ap.add_argument("--no-generate", dest="generate", action="store_false",
+                    help="skip the end-to-end greedy generate on the random-init Qwen3-VL-2B-shaped model")
+    ap.add_argument("--only", choices=["decode", "split_kv", "prefill", "vit", "generate"], default=None,
                     help="run one workload (profiling)")
     ap.add_argument("--layers", type=int, default=LAYERS, help="decode layers per step (28 = Qwen3-VL-2B)")
     args = ap.parse_args(argv)
@@ -542,6 +558,8 @@ def main(argv=None) -> int:
         result["split_kv_cfg5"] = run_split_kv(args, world, rank, device)
     if args.secondary and only in (None, "prefill", "vit"):
         result.update(run_fmha_secondary(args, world, device, peaks, only))
+    if world == 1 and ((args.generate and only is None) or only == "generate"):
+        result["generate_cfg4"] = run_generate(device)
     line = None
     if rank == 0:
         line = {"metric": METRIC, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
