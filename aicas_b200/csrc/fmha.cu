@@ -37,7 +37,7 @@ namespace aicas {
 namespace {
 
 constexpr int kBM = 128;  // query rows per tile (MMA M)
-constexpr int kThreads = 384;
+constexpr int kThreads = 384;  // warpgroup 0: producer, MMA (2 warps idle); warpgroups 1, 2: softmax
 
 struct FmhaArgs {
   CUtensorMap tm_q, tm_k, tm_v;  // 4-D, box {64 elements, 128 (Q) or BN (K, V) rows, 1 head, 1 batch}
@@ -318,140 +318,149 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
     *abort_flag = 1;
   }
   __syncthreads();
-  if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
-    if (lane == 0 && !*abort_flag) {
-      tma_prefetch_desc(&a.tm_q);
-      tma_prefetch_desc(&a.tm_k);
-      tma_prefetch_desc(&a.tm_v);
-      mbar_arrive_expect_tx(q_full, 2 * Lay::kQTile);
-      for (int t = 0; t < 2; ++t)
-        for (int bx = 0; bx < D / 64; ++bx)
-          tma_tile(sb + Lay::kQ + t * Lay::kQTile + bx * (kBM * 128), &a.tm_q, a.q_rows_first, bx * 64,
-                   q_base + (t ? row1 : row0), t ? head1 : head0, b, q_full);
-      int issued = 0;
-      for (int idx = 0; idx < 2 * n_kv; ++idx) {
-        // idx -> tile: 0 is K0, then K(j+1), V(j) pairs, the last V alone
-        bool is_v;
-        int j;
-        if (idx == 0) {
-          is_v = false;
-          j = 0;
-        } else if (idx == 2 * n_kv - 1) {
-          is_v = true;
-          j = n_kv - 1;
-        } else {
-          is_v = (idx & 1) == 0;
-          j = is_v ? (idx - 2) / 2 : (idx + 1) / 2;
+  if (warp < 4) {
+    // register split: 104 per thread here, 200 in the softmax warpgroups
+    // (128 x 104 + 256 x 200 = 64512 = 384 x 168, the launch allocation)
+    tc::regs_dec<104>();
+    if (warp == 0) {
+      // ------------------------------------------------------------ TMA producer
+      if (lane == 0 && !*abort_flag) {
+        tma_prefetch_desc(&a.tm_q);
+        tma_prefetch_desc(&a.tm_k);
+        tma_prefetch_desc(&a.tm_v);
+        mbar_arrive_expect_tx(q_full, 2 * Lay::kQTile);
+        for (int t = 0; t < 2; ++t)
+          for (int bx = 0; bx < D / 64; ++bx)
+            tma_tile(sb + Lay::kQ + t * Lay::kQTile + bx * (kBM * 128), &a.tm_q, a.q_rows_first, bx * 64,
+                     q_base + (t ? row1 : row0), t ? head1 : head0, b, q_full);
+        int issued = 0;
+        for (int idx = 0; idx < 2 * n_kv; ++idx) {
+          // idx -> tile: 0 is K0, then K(j+1), V(j) pairs, the last V alone
+          bool is_v;
+          int j;
+          if (idx == 0) {
+            is_v = false;
+            j = 0;
+          } else if (idx == 2 * n_kv - 1) {
+            is_v = true;
+            j = n_kv - 1;
+          } else {
+            is_v = (idx & 1) == 0;
+            j = is_v ? (idx - 2) / 2 : (idx + 1) / 2;
+          }
+          const int s = idx % NS, u = idx / NS;
+          if (u > 0 && !mbar_wait(kv_empty(s), (u - 1) & 1, abort_flag, a.err)) break;
+          mbar_arrive_expect_tx(kv_full(s), Lay::kKVTile);
+          for (int bx = 0; bx < D / 64; ++bx)
+            tma_tile(sb + Lay::kKV + s * Lay::kKVTile + bx * (kBN * 128), is_v ? &a.tm_v : &a.tm_k,
+                     is_v ? a.v_rows_first : a.k_rows_first, bx * 64, k_base + j * kBN, kvh, b, kv_full(s));
+          ++issued;
         }
-        const int s = idx % NS, u = idx / NS;
-        if (u > 0 && !mbar_wait(kv_empty(s), (u - 1) & 1, abort_flag, a.err)) break;
-        mbar_arrive_expect_tx(kv_full(s), Lay::kKVTile);
-        for (int bx = 0; bx < D / 64; ++bx)
-          tma_tile(sb + Lay::kKV + s * Lay::kKVTile + bx * (kBN * 128), is_v ? &a.tm_v : &a.tm_k,
-                   is_v ? a.v_rows_first : a.k_rows_first, bx * 64, k_base + j * kBN, kvh, b, kv_full(s));
-        ++issued;
+        if (*abort_flag) {  // let our own copies land before the CTA can retire
+          mbar_wait(q_full, 0, nullptr, a.err);
+          for (int idx = max(0, issued - NS); idx < issued; ++idx)
+            mbar_wait(kv_full(idx % NS), (idx / NS) & 1, nullptr, a.err);
+        }
       }
-      if (*abort_flag) {  // let our own copies land before the CTA can retire
-        mbar_wait(q_full, 0, nullptr, a.err);
-        for (int idx = max(0, issued - NS); idx < issued; ++idx)
-          mbar_wait(kv_full(idx % NS), (idx / NS) & 1, nullptr, a.err);
-      }
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issue (one thread)
-    if (lane == 0) {
-      constexpr uint32_t kIdS = tc::idesc_f16(kBF16, kBM, kBN, false, false);
-      constexpr uint32_t kIdPV = tc::idesc_f16(kBF16, kBM, D, false, true);
-      // Descriptors are built once.  A descriptor depends on its tile's address
-      // only through the 14-bit start-address field (address >> 4, below 2^14
-      // for every shared-memory address here), so moving to another tile or
-      // k-step is one 64-bit add of a constant: the issuing thread spends its
-      // time issuing products, not rebuilding descriptors.
-      const uint64_t dq0 = tc::smem_desc_sw128(sb + Lay::kQ, 16, 1024);
-      const uint64_t dk0 = tc::smem_desc_sw128(sb + Lay::kKV, 16, 1024);
-      const uint64_t dv0 = tc::smem_desc_sw128(sb + Lay::kKV, kBN * 128, 1024);
-      auto issue_s = [&](int stage, int t) {
-        const uint64_t qa = dq0 + ((uint64_t)(t * Lay::kQTile) >> 4);
-        const uint64_t kb = dk0 + ((uint64_t)(stage * Lay::kKVTile) >> 4);
-        const uint32_t dst = tmem + t * kBN;
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          tc::mma_f16_ss(dst, qa + (uint64_t)(((kk >> 2) * (kBM * 128) + (kk & 3) * 32) >> 4),
-                         kb + (uint64_t)(((kk >> 2) * (kBN * 128) + (kk & 3) * 32) >> 4), kIdS, kk > 0 ? 1u : 0u);
-      };
-      const uint64_t dp0 = tc::smem_desc_sw128(sb + Lay::kP, 16, 1024);
-      auto issue_pv = [&](int j, int stage, int t) {
-        const uint64_t vb = dv0 + ((uint64_t)(stage * Lay::kKVTile) >> 4);
-        const uint32_t dst = tmem + Lay::kColO + t * D;
-        if constexpr (Lay::kPTmem) {
-          const uint32_t pa = tmem + Lay::kColP + t * (kBN / 2);
-#pragma unroll
-          for (int kk = 0; kk < kBN / 16; ++kk)
-            tc::mma_f16_ts(dst, pa + kk * 8, vb + (uint64_t)((kk * (16 * 128)) >> 4), kIdPV,
-                           (j > 0 || kk > 0) ? 1u : 0u);
-        } else {
-          const uint64_t pa = dp0 + ((uint64_t)(t * Lay::kPTile) >> 4);
-#pragma unroll
-          for (int kk = 0; kk < kBN / 16; ++kk)
-            tc::mma_f16_ss(dst, pa + (uint64_t)(((kk >> 2) * (kBM * 128) + (kk & 3) * 32) >> 4),
-                           vb + (uint64_t)((kk * (16 * 128)) >> 4), kIdPV, (j > 0 || kk > 0) ? 1u : 0u);
-        }
-      };
-      bool ok = !*abort_flag && mbar_wait(q_full, 0, abort_flag, a.err);
-      if (ok && n_kv > 0) {
-        ok = mbar_wait(kv_full(0), 0, abort_flag, a.err);
-        if (ok) {
-          tc::fence_after_sync();
-          issue_s(0, 0);
-          tc::commit(s_full(0));
-          issue_s(0, 1);
-          tc::commit(s_full(1));
-          tc::commit(kv_empty(0));
-        }
-        for (int j = 0; ok && j < n_kv; ++j) {
-          const int iv = kv_load_index_v(j, n_kv), ik = kv_load_index_k(j + 1);
-          const int sv = iv % NS, sk = ik % NS;
-          const bool more = j + 1 < n_kv;
-          // Per-tile order, as the softmax groups release their inputs:
-          // S(j+1,0) as soon as group 0 has READ S(j,0) (not after its softmax),
-          // PV(j,0) once P(j,0) is written, then the same for tile 1.
-          if (more) {
-            ok = mbar_wait(kv_full(sk), (ik / NS) & 1, abort_flag, a.err) &&
-                 mbar_wait(s_free(0), j & 1, abort_flag, a.err);
-            if (!ok) break;
+    } else if (warp == 1) {
+      // ------------------------------------------------------------ MMA issue (one thread)
+      if (lane == 0) {
+        constexpr uint32_t kIdS = tc::idesc_f16(kBF16, kBM, kBN, false, false);
+        constexpr uint32_t kIdPV = tc::idesc_f16(kBF16, kBM, D, false, true);
+        // Descriptors are built once.  A descriptor depends on its tile's address
+        // only through the 14-bit start-address field (address >> 4, below 2^14
+        // for every shared-memory address here), so moving to another tile or
+        // k-step is one 64-bit add of a constant: the issuing thread spends its
+        // time issuing products, not rebuilding descriptors.
+        const uint64_t dq0 = tc::smem_desc_sw128(sb + Lay::kQ, 16, 1024);
+        const uint64_t dk0 = tc::smem_desc_sw128(sb + Lay::kKV, 16, 1024);
+        const uint64_t dv0 = tc::smem_desc_sw128(sb + Lay::kKV, kBN * 128, 1024);
+        auto issue_s = [&](int stage, int t) {
+          const uint64_t qa = dq0 + ((uint64_t)(t * Lay::kQTile) >> 4);
+          const uint64_t kb = dk0 + ((uint64_t)(stage * Lay::kKVTile) >> 4);
+          const uint32_t dst = tmem + t * kBN;
+  #pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk)
+            tc::mma_f16_ss(dst, qa + (uint64_t)(((kk >> 2) * (kBM * 128) + (kk & 3) * 32) >> 4),
+                           kb + (uint64_t)(((kk >> 2) * (kBN * 128) + (kk & 3) * 32) >> 4), kIdS, kk > 0 ? 1u : 0u);
+        };
+        const uint64_t dp0 = tc::smem_desc_sw128(sb + Lay::kP, 16, 1024);
+        auto issue_pv = [&](int j, int stage, int t) {
+          const uint64_t vb = dv0 + ((uint64_t)(stage * Lay::kKVTile) >> 4);
+          const uint32_t dst = tmem + Lay::kColO + t * D;
+          if constexpr (Lay::kPTmem) {
+            const uint32_t pa = tmem + Lay::kColP + t * (kBN / 2);
+  #pragma unroll
+            for (int kk = 0; kk < kBN / 16; ++kk)
+              tc::mma_f16_ts(dst, pa + kk * 8, vb + (uint64_t)((kk * (16 * 128)) >> 4), kIdPV,
+                             (j > 0 || kk > 0) ? 1u : 0u);
+          } else {
+            const uint64_t pa = dp0 + ((uint64_t)(t * Lay::kPTile) >> 4);
+  #pragma unroll
+            for (int kk = 0; kk < kBN / 16; ++kk)
+              tc::mma_f16_ss(dst, pa + (uint64_t)(((kk >> 2) * (kBM * 128) + (kk & 3) * 32) >> 4),
+                             vb + (uint64_t)((kk * (16 * 128)) >> 4), kIdPV, (j > 0 || kk > 0) ? 1u : 0u);
+          }
+        };
+        bool ok = !*abort_flag && mbar_wait(q_full, 0, abort_flag, a.err);
+        if (ok && n_kv > 0) {
+          ok = mbar_wait(kv_full(0), 0, abort_flag, a.err);
+          if (ok) {
             tc::fence_after_sync();
-            issue_s(sk, 0);
+            issue_s(0, 0);
             tc::commit(s_full(0));
+            issue_s(0, 1);
+            tc::commit(s_full(1));
+            tc::commit(kv_empty(0));
           }
-          ok = mbar_wait(kv_full(sv), (iv / NS) & 1, abort_flag, a.err) &&
-               mbar_wait(p_full(0), j & 1, abort_flag, a.err);
-          if (!ok) break;
-          tc::fence_after_sync();
-          issue_pv(j, sv, 0);
-          tc::commit(o_full(0));
-          if (more) {
-            ok = mbar_wait(s_free(1), j & 1, abort_flag, a.err);
+          for (int j = 0; ok && j < n_kv; ++j) {
+            const int iv = kv_load_index_v(j, n_kv), ik = kv_load_index_k(j + 1);
+            const int sv = iv % NS, sk = ik % NS;
+            const bool more = j + 1 < n_kv;
+            // Per-tile order, as the softmax groups release their inputs:
+            // S(j+1,0) as soon as group 0 has READ S(j,0) (not after its softmax),
+            // PV(j,0) once P(j,0) is written, then the same for tile 1.
+            if (more) {
+              ok = mbar_wait(kv_full(sk), (ik / NS) & 1, abort_flag, a.err) &&
+                   mbar_wait(s_free(0), j & 1, abort_flag, a.err);
+              if (!ok) break;
+              tc::fence_after_sync();
+              issue_s(sk, 0);
+              tc::commit(s_full(0));
+            }
+            ok = mbar_wait(kv_full(sv), (iv / NS) & 1, abort_flag, a.err) &&
+                 mbar_wait(p_full(0), j & 1, abort_flag, a.err);
             if (!ok) break;
             tc::fence_after_sync();
-            issue_s(sk, 1);
-            tc::commit(s_full(1));
-            tc::commit(kv_empty(sk));
+            issue_pv(j, sv, 0);
+            tc::commit(o_full(0));
+            if (more) {
+              ok = mbar_wait(s_free(1), j & 1, abort_flag, a.err);
+              if (!ok) break;
+              tc::fence_after_sync();
+              issue_s(sk, 1);
+              tc::commit(s_full(1));
+              tc::commit(kv_empty(sk));
+            }
+            ok = mbar_wait(p_full(1), j & 1, abort_flag, a.err);
+            if (!ok) break;
+            tc::fence_after_sync();
+            issue_pv(j, sv, 1);
+            tc::commit(o_full(1));
+            tc::commit(kv_empty(sv));
           }
-          ok = mbar_wait(p_full(1), j & 1, abort_flag, a.err);
-          if (!ok) break;
-          tc::fence_after_sync();
-          issue_pv(j, sv, 1);
-          tc::commit(o_full(1));
-          tc::commit(kv_empty(sv));
         }
+        // all products issued so far have completed before the CTA tears down
+        tc::commit(mma_done);
+        mbar_wait(mma_done, 0, nullptr, a.err);
       }
-      // all products issued so far have completed before the CTA tears down
-      tc::commit(mma_done);
-      mbar_wait(mma_done, 0, nullptr, a.err);
     }
-  } else if (warp >= 4) {
+  } else {
     // ------------------------------------------------------------ softmax + epilogue
+    // warpgroup 1 owns query tile 0, warpgroup 2 tile 1; a warp may only touch
+    // the TMEM lanes of its rank within its warpgroup (warp % 4), which is the
+    // quarter of the tile's rows it owns
+    tc::regs_inc<200>();
     const int t = (warp - 4) >> 2;
     const int qw = warp & 3;
     const int r = qw * 32 + lane;
@@ -517,8 +526,42 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
         m_ref = mx;
       }
       const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
-      // the P columns and O are free once PV(j-1) of this tile has completed (O
-      // is rescaled below, after P is written, when this row's reference moved)
+      // P = 2^(s*c - m) for the whole row, packed to 16-bit pairs in registers
+      // (the S registers are consumed as P fills): none of it waits for the
+      // previous P.V product, which still reads this tile's P buffer.  Pairs
+      // are scaled with one f32x2 FMA; on tiles without masked entries
+      // kPolyPairs of every 8 pairs take the polynomial exponential, the rest
+      // ex2.approx; partial sums in f32x2 accumulators.
+      uint64_t rs2[2] = {f2(0.f, 0.f), f2(0.f, 0.f)};
+      const uint64_t c2 = f2(c, c), nm2 = f2(-m_use, -m_use);
+      uint32_t pk[kBN / 2];
+      if (mask) {
+#pragma unroll
+        for (int e = 0; e < kBN / 2; ++e) {
+          float x0, x1;
+          unf2(ffma2(f2(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1])), c2, nm2), x0, x1);
+          const float p0 = ex2(x0), p1 = ex2(x1);
+          rs2[e & 1] = fadd2(rs2[e & 1], f2(p0, p1));
+          pk[e] = pack2<T>(p0, p1);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < kBN / 2; ++e) {
+          const uint64_t x2 = ffma2(f2(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1])), c2, nm2);
+          float p0, p1;
+          if ((e & 7) < kPolyPairs) {
+            unf2(exp2_poly2(x2), p0, p1);
+          } else {
+            float x0, x1;
+            unf2(x2, x0, x1);
+            p0 = ex2(x0);
+            p1 = ex2(x1);
+          }
+          rs2[e & 1] = fadd2(rs2[e & 1], f2(p0, p1));
+          pk[e] = pack2<T>(p0, p1);
+        }
+      }
+      // the P buffer and O are free once PV(j-1) of this tile has completed
       if (j > 0) {
         if (!warp_wait(o_full(t), (j - 1) & 1, abort_flag, a.err)) {
           ok = false;
@@ -526,53 +569,18 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
         }
         tc::fence_after_sync();
       }
-      // P = 2^(s*c - m), packed to 16-bit pairs and stored 64 keys at a time to
-      // this row's lane of the P columns (head_dim 64) or its smem row (128).  Pairs
-      // are scaled with one f32x2 FMA; on tiles without masked entries
-      // kPolyPairs of every 8 pairs take the polynomial exponential, the rest
-      // ex2.approx; partial sums in f32x2 accumulators.
-      uint64_t rs2[2] = {f2(0.f, 0.f), f2(0.f, 0.f)};
-      const uint64_t c2 = f2(c, c), nm2 = f2(-m_use, -m_use);
 #pragma unroll
       for (int h = 0; h < kBN / 64; ++h) {
-        uint32_t pk[32];
-        if (mask) {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int i = 64 * h + 2 * e;
-            float x0, x1;
-            unf2(ffma2(f2(__uint_as_float(v[i]), __uint_as_float(v[i + 1])), c2, nm2), x0, x1);
-            const float p0 = ex2(x0), p1 = ex2(x1);
-            rs2[e & 1] = fadd2(rs2[e & 1], f2(p0, p1));
-            pk[e] = pack2<T>(p0, p1);
-          }
-        } else {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int i = 64 * h + 2 * e;
-            const uint64_t x2 = ffma2(f2(__uint_as_float(v[i]), __uint_as_float(v[i + 1])), c2, nm2);
-            float p0, p1;
-            if ((e & 7) < kPolyPairs) {
-              unf2(exp2_poly2(x2), p0, p1);
-            } else {
-              float x0, x1;
-              unf2(x2, x0, x1);
-              p0 = ex2(x0);
-              p1 = ex2(x1);
-            }
-            rs2[e & 1] = fadd2(rs2[e & 1], f2(p0, p1));
-            pk[e] = pack2<T>(p0, p1);
-          }
-        }
         if constexpr (Lay::kPTmem) {
-          tc::tmem_st32(tl + col_p + 32 * h, pk);
+          tc::tmem_st32(tl + col_p + 32 * h, pk + 32 * h);
         } else {
           // K-major 128B-swizzled P tile: 16-byte chunk c of row r at c ^ (r % 8)
           uint8_t* sub = prow + h * (kBM * 128);
 #pragma unroll
           for (int ch = 0; ch < 8; ++ch)
             *reinterpret_cast<uint4*>(sub + ((ch ^ (r & 7)) << 4)) =
-                make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
+                make_uint4(pk[32 * h + 4 * ch], pk[32 * h + 4 * ch + 1], pk[32 * h + 4 * ch + 2],
+                           pk[32 * h + 4 * ch + 3]);
         }
       }
       float rs4[4];
