@@ -1,6 +1,6 @@
 // Shared device helpers for the sm_100a kernels: element conversion, mbarriers
-// with bounded waits, bulk / tensor copies (TMA, never multicast) and the
-// device-side error word.
+// with bounded waits, bulk / tensor copies (TMA into this CTA's own shared
+// memory only) and the device-side error word.
 #pragma once
 
 #include <cuda.h>
@@ -144,7 +144,7 @@ __device__ __forceinline__ uint64_t l2_policy_evict_last() {
   return pol;
 }
 
-// Tiled tensor copies through a CUtensorMap (4-D), no multicast.
+// Tiled tensor copies through a CUtensorMap (4-D) into this CTA's shared memory.
 __device__ __forceinline__ void tma_load_4d(uint32_t dst_smem, const CUtensorMap* map, int c0,
                                             int c1, int c2, int c3, uint32_t bar) {
   asm volatile(

@@ -11,8 +11,8 @@
 //   * one CTA per (request, KV head, split of the cache); the whole GQA group of
 //     query heads is served from ONE copy of each K/V tile (the reference streams
 //     the KV head once per query head);
-//   * a producer warp streams 16 KB K and V tiles with cp.async.bulk (TMA, no
-//     multicast, L2 evict-first) into a 3-stage mbarrier ring;
+//   * a producer warp streams 16 KB K and V tiles with cp.async.bulk (TMA into
+//     this CTA's shared memory, L2 evict-first) into a 3-stage mbarrier ring;
 //   * 4 consumer warps each own a quarter of every tile: 16-byte vector reads
 //     from shared memory, a reduce-scatter of the q.k partial sums over the lanes
 //     of a token, warp-shuffle maxima, per-warp online softmax;
