@@ -25,12 +25,14 @@ ERR_WORKSPACE = 4
 
 DEVERR_WAIT_TIMEOUT = 1
 DEVERR_TMEM = 2
+DEVERR_PEER_TIMEOUT = 4
 
 CAP_DECODE = 1
 CAP_MERGE = 2
 CAP_PREFILL_TCGEN05 = 4
 CAP_VARLEN_TCGEN05 = 8
 CAP_ROPE_APPEND = 16
+CAP_PEER_EXCHANGE = 32
 
 _i64 = ctypes.c_int64
 _i32 = ctypes.c_int32
@@ -56,6 +58,19 @@ class MergeParams(ctypes.Structure):
         ("partial_o", _vp), ("partial_lse", _vp), ("out", _vp), ("lse", _vp),
         ("o_stride_b", _i64), ("o_stride_h", _i64),
         ("num_partials", _i32), ("batch", _i32), ("num_heads", _i32), ("head_dim", _i32),
+        ("dtype", _i32),
+    ]
+
+
+MAX_EXCHANGE_RANKS = 8
+IPC_HANDLE_BYTES = 64
+
+
+class ExchangeParams(ctypes.Structure):
+    _fields_ = [
+        ("peers", _vp * MAX_EXCHANGE_RANKS), ("partial_o", _vp), ("partial_lse", _vp), ("out", _vp), ("lse", _vp),
+        ("o_stride_b", _i64), ("o_stride_h", _i64),
+        ("world", _i32), ("rank", _i32), ("batch", _i32), ("num_heads", _i32), ("head_dim", _i32),
         ("dtype", _i32),
     ]
 
@@ -96,6 +111,12 @@ EXPORTS = {
     "aicas_decode_gqa": (ctypes.c_int, [ctypes.POINTER(DecodeParams), _vp, ctypes.c_size_t, _vp]),
     "aicas_decode_gqa_noalloc": (ctypes.c_int, [ctypes.POINTER(DecodeParams), _vp]),
     "aicas_merge_partials": (ctypes.c_int, [ctypes.POINTER(MergeParams), _vp]),
+    "aicas_exchange_buffer_bytes": (ctypes.c_size_t, [_i32, _i32, _i32, _i32]),
+    "aicas_peer_buffer_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(_vp), _vp]),
+    "aicas_peer_buffer_free": (ctypes.c_int, [_vp]),
+    "aicas_peer_buffer_open": (ctypes.c_int, [_vp, ctypes.POINTER(_vp)]),
+    "aicas_peer_buffer_close": (ctypes.c_int, [_vp]),
+    "aicas_exchange_merge": (ctypes.c_int, [ctypes.POINTER(ExchangeParams), _vp]),
     "aicas_prefill_gqa_causal": (ctypes.c_int, [ctypes.POINTER(FmhaParams), _vp]),
     "aicas_varlen_attention": (ctypes.c_int, [ctypes.POINTER(FmhaParams), _vp]),
     "aicas_rope_kv_append": (ctypes.c_int, [ctypes.POINTER(RopeAppendParams), _vp]),

@@ -20,7 +20,8 @@ struct DecodeArgs {
   int max_splits;
   float* ws_o;            // [B*Hkv, max_splits, G, D]
   float* ws_lse;          // [B*Hkv, max_splits, G]
-  unsigned int* ws_count; // [B*Hkv]
+  unsigned int* ws_count; // [B*Hkv] split counters (null: no split-KV workspace)
+  unsigned int* ws_sched; // [2] work-item counter, finished-CTA counter (with a workspace)
   unsigned int* err;      // device error word
 };
 
@@ -43,6 +44,20 @@ struct RopeArgs {
   int64_t cs_sb, cs_ss;
   int64_t kc_sb, kc_sh, vc_sb, vc_sh;
   int batch, hq, hkv, seq, hd, cap;
+};
+
+constexpr int kMaxExchangeRanks = 8;
+
+struct ExchangeArgs {
+  void* peers[kMaxExchangeRanks];  // every rank's exchange buffer, mapped into this device
+  const float* po;                 // local partial [B*H*D] fp32
+  const float* plse;               // local partial LSE [B*H] fp32 (base 2)
+  void* out;
+  float* lse;
+  int64_t o_sb, o_sh;
+  int world, rank, batch, heads, hd;
+  int slot_floats;
+  unsigned int* err;               // device error word
 };
 
 struct MergeArgs {

@@ -1,6 +1,7 @@
 // C ABI entry points: argument validation, launch planning and error reporting.
 // Nothing here allocates device memory or synchronises the device (except the
-// explicit health query aicas_device_error_flags).
+// one-time peer-buffer set-up calls aicas_peer_buffer_alloc/free, and
+// the explicit health query aicas_device_error_flags).
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
@@ -18,6 +19,10 @@ struct RopeArgs;
 cudaError_t launch_rope_append(int dtype, int cs_dtype, const RopeArgs& a, cudaStream_t st);
 struct MergeArgs;
 cudaError_t launch_merge(int dtype, const MergeArgs& a, cudaStream_t st);
+struct ExchangeArgs;
+cudaError_t launch_exchange_merge(int dtype, const ExchangeArgs& a, cudaStream_t st);
+size_t exchange_slot_floats(int batch, int heads, int head_dim);
+size_t exchange_buffer_bytes(int world, int batch, int heads, int head_dim);
 
 }  // namespace aicas
 
@@ -84,9 +89,12 @@ unsigned int* device_error_word() {
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
-// Split-KV workspace: [counters: kMaxSplitUnits x u32][partial o][partial lse].
-constexpr int kMaxSplitUnits = 262144;
-constexpr size_t kCounterBytes = (size_t)kMaxSplitUnits * sizeof(unsigned int);
+// Split-KV workspace: [counters: 1 MiB][partial o][partial lse].  The counter
+// region holds kMaxSplitUnits split counters and, in its last 64 bytes, the
+// persistent kernel's work-item and finished-CTA counters.
+constexpr size_t kCounterBytes = (size_t)1 << 20;
+constexpr size_t kSchedOffset = kCounterBytes - 64;
+constexpr int kMaxSplitUnits = (int)(kSchedOffset / sizeof(unsigned int));
 
 // Split-KV plan shared by aicas_decode_workspace_bytes and aicas_decode_gqa.
 struct DecodePlan {
@@ -102,10 +110,22 @@ int plan_decode(const aicas_decode_params* p, DecodePlan* out) {
     return fail(AICAS_ERR_UNSUPPORTED, "split_tokens=%d must be 0 or a positive multiple of %d",
                 p->split_tokens, tile);
   if (split == 0) {
-    // enough work units for ~8 resident waves of 2 CTAs per SM, in whole tiles
-    const int64_t total = (int64_t)p->batch * p->num_kv_heads * (int64_t)(p->kv_capacity > 0 ? p->kv_capacity : 1);
-    const int64_t target = (int64_t)sm_count() * 2 * 8;
-    int64_t s = (total + target - 1) / target;
+    // Persistent CTAs (2 per SM) take the splits as work items.  Every item
+    // boundary costs a CTA a few microseconds (partial write, counter, merge),
+    // so items are as long as balance allows: with few (request, KV head)
+    // pairs, about one item per resident CTA (one wave, no boundaries); with
+    // many pairs of ragged lengths, about five items per CTA so that the
+    // dynamic hand-out can even out the lengths.
+    const int64_t cap = p->kv_capacity > 0 ? p->kv_capacity : 1;
+    const int64_t pairs = (int64_t)p->batch * p->num_kv_heads;
+    const int64_t resident = (int64_t)sm_count() * 2;
+    int64_t s;
+    if (2 * pairs <= resident) {
+      const int64_t per_pair = resident / pairs;
+      s = (cap + per_pair - 1) / per_pair;
+    } else {
+      s = (cap * pairs + 5 * resident - 1) / (5 * resident);
+    }
     s = (s + tile - 1) / tile * tile;
     if (s < 4 * tile) s = 4 * tile;
     if (s > 16384) s = 16384;
@@ -235,7 +255,8 @@ extern "C" {
 const char* aicas_version(void) { return "aicas_b200 0.1.0 sm_100a abi 1"; }
 
 uint32_t aicas_capabilities(void) {
-  return AICAS_CAP_DECODE | AICAS_CAP_MERGE | AICAS_CAP_ROPE_APPEND | aicas::fmha_capabilities();
+  return AICAS_CAP_DECODE | AICAS_CAP_MERGE | AICAS_CAP_ROPE_APPEND | AICAS_CAP_PEER_EXCHANGE |
+         aicas::fmha_capabilities();
 }
 
 const char* aicas_last_error(void) { return g_err; }
@@ -287,6 +308,7 @@ int aicas_decode_gqa(const aicas_decode_params* p, void* workspace, size_t works
   a.ws_o = plan.ws_bytes ? reinterpret_cast<float*>(ws + plan.ws_o_off) : nullptr;
   a.ws_lse = plan.ws_bytes ? reinterpret_cast<float*>(ws + plan.ws_lse_off) : nullptr;
   a.ws_count = plan.ws_bytes ? reinterpret_cast<unsigned int*>(ws + plan.ws_count_off) : nullptr;
+  a.ws_sched = plan.ws_bytes ? reinterpret_cast<unsigned int*>(ws + kSchedOffset) : nullptr;
   a.err = device_error_word();
   cudaError_t e = aicas::launch_decode(p->dtype, p->head_dim, p->num_q_heads / p->num_kv_heads, a,
                                        static_cast<cudaStream_t>(stream));
@@ -312,8 +334,11 @@ int aicas_decode_gqa_noalloc(const aicas_decode_params* p, void* stream) {
     // the split counters of this call must start at zero: clear them (a call
     // that was cut short could have left some behind); partials need no clearing
     const size_t counter_bytes = (size_t)p->batch * p->num_kv_heads * sizeof(unsigned int);
-    const cudaError_t e = cudaMemsetAsync(static_cast<uint8_t*>(scratch) + plan.ws_count_off, 0, counter_bytes,
-                                          static_cast<cudaStream_t>(stream));
+    cudaError_t e = cudaMemsetAsync(static_cast<uint8_t*>(scratch) + plan.ws_count_off, 0, counter_bytes,
+                                    static_cast<cudaStream_t>(stream));
+    // and so must the work-item counters of the persistent kernel
+    if (e == cudaSuccess)
+      e = cudaMemsetAsync(static_cast<uint8_t*>(scratch) + kSchedOffset, 0, 64, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "aicas_decode_gqa_noalloc: clearing the split counters");
   }
   return aicas_decode_gqa(p, scratch, scratch != nullptr ? kNoAllocScratchBytes : 0, stream);
@@ -332,6 +357,88 @@ int aicas_merge_partials(const aicas_merge_params* p, void* stream) {
   a.np = p->num_partials; a.batch = p->batch; a.heads = p->num_heads; a.hd = p->head_dim;
   cudaError_t e = aicas::launch_merge(p->dtype, a, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "merge launch");
+  return AICAS_OK;
+}
+
+size_t aicas_exchange_buffer_bytes(int32_t world, int32_t batch, int32_t num_heads, int32_t head_dim) {
+  if (world < 1 || world > AICAS_MAX_EXCHANGE_RANKS || batch < 1 || num_heads < 1 || head_dim < 1) return 0;
+  return aicas::exchange_buffer_bytes(world, batch, num_heads, head_dim);
+}
+
+int aicas_peer_buffer_alloc(size_t bytes, void** ptr, void* ipc_handle) {
+  if (ptr == nullptr || ipc_handle == nullptr || bytes == 0)
+    return fail(AICAS_ERR_INVALID, "ptr, ipc_handle and a non-zero size are required");
+  static_assert(sizeof(cudaIpcMemHandle_t) == AICAS_IPC_HANDLE_BYTES, "IPC handle size");
+  *ptr = nullptr;
+  void* d = nullptr;
+  cudaError_t e = cudaMalloc(&d, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "aicas_peer_buffer_alloc: cudaMalloc");
+  e = cudaMemset(d, 0, bytes);  // flags and epoch start at zero
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, d);
+  if (e != cudaSuccess) {
+    cudaFree(d);
+    return cuda_fail(e, "aicas_peer_buffer_alloc: zeroing / IPC handle");
+  }
+  memcpy(ipc_handle, &h, sizeof(h));
+  *ptr = d;
+  return AICAS_OK;
+}
+
+int aicas_peer_buffer_free(void* ptr) {
+  if (ptr == nullptr) return AICAS_OK;
+  const cudaError_t e = cudaFree(ptr);
+  return e == cudaSuccess ? AICAS_OK : cuda_fail(e, "aicas_peer_buffer_free");
+}
+
+int aicas_peer_buffer_open(const void* ipc_handle, void** ptr) {
+  if (ptr == nullptr || ipc_handle == nullptr) return fail(AICAS_ERR_INVALID, "ipc_handle and ptr are required");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  *ptr = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  return e == cudaSuccess ? AICAS_OK : cuda_fail(e, "aicas_peer_buffer_open: cudaIpcOpenMemHandle");
+}
+
+int aicas_peer_buffer_close(void* ptr) {
+  if (ptr == nullptr) return AICAS_OK;
+  const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  return e == cudaSuccess ? AICAS_OK : cuda_fail(e, "aicas_peer_buffer_close");
+}
+
+int aicas_exchange_merge(const aicas_exchange_params* p, void* stream) {
+  if (p == nullptr) return fail(AICAS_ERR_INVALID, "params is NULL");
+  if (p->world < 1 || p->world > AICAS_MAX_EXCHANGE_RANKS || p->rank < 0 || p->rank >= p->world)
+    return fail(AICAS_ERR_INVALID, "rank %d of world %d (at most %d ranks)", p->rank, p->world,
+                AICAS_MAX_EXCHANGE_RANKS);
+  if (p->partial_o == nullptr || p->partial_lse == nullptr || p->out == nullptr)
+    return fail(AICAS_ERR_INVALID, "partial_o, partial_lse and out must be non-NULL");
+  for (int r = 0; r < p->world; ++r)
+    if (p->peers[r] == nullptr || (reinterpret_cast<uintptr_t>(p->peers[r]) & 255u) != 0)
+      return fail(AICAS_ERR_INVALID, "exchange buffer of rank %d is NULL or not 256-byte aligned", r);
+  if (elem_bytes(p->dtype) == 0) return fail(AICAS_ERR_UNSUPPORTED, "unknown dtype %d", p->dtype);
+  if (p->batch < 1 || p->num_heads < 1 || p->head_dim < 4 || p->head_dim > 1024 || (p->head_dim & 3))
+    return fail(AICAS_ERR_INVALID, "bad sizes (head_dim must be a multiple of 4)");
+  if ((reinterpret_cast<uintptr_t>(p->partial_o) & 15u) != 0)
+    return fail(AICAS_ERR_INVALID, "partial_o must be 16-byte aligned");
+  aicas::ExchangeArgs a;
+  memset(&a, 0, sizeof(a));
+  for (int r = 0; r < p->world; ++r) a.peers[r] = p->peers[r];
+  a.po = p->partial_o;
+  a.plse = p->partial_lse;
+  a.out = p->out;
+  a.lse = p->lse;
+  a.o_sb = p->o_stride_b;
+  a.o_sh = p->o_stride_h;
+  a.world = p->world;
+  a.rank = p->rank;
+  a.batch = p->batch;
+  a.heads = p->num_heads;
+  a.hd = p->head_dim;
+  a.slot_floats = (int)aicas::exchange_slot_floats(p->batch, p->num_heads, p->head_dim);
+  a.err = device_error_word();
+  const cudaError_t e = aicas::launch_exchange_merge(p->dtype, a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "exchange merge launch");
   return AICAS_OK;
 }
 

@@ -8,9 +8,10 @@
 // and LSE = m + log2(l) in the base-2 scaled domain (:141).
 //
 // B200 design:
-//   * one CTA per (request, KV head, split of the cache); the whole GQA group of
-//     query heads is served from ONE copy of each K/V tile (the reference streams
-//     the KV head once per query head);
+//   * work items are (request, KV head, split of the cache), run by persistent
+//     CTAs (see decode_gqa_kernel); the whole GQA group of query heads is served
+//     from ONE copy of each K/V tile (the reference streams the KV head once per
+//     query head);
 //   * a producer warp streams 16 KB K and V tiles with cp.async.bulk (TMA into
 //     this CTA's shared memory, L2 evict-first) into a 3-stage mbarrier ring;
 //   * 4 consumer warps each own a quarter of every tile: 16-byte vector reads
@@ -44,16 +45,57 @@ struct DecodeCfg {
   static constexpr int kRV = kNV >> kHalve;            // values kept per lane (multiple of G)
   static constexpr int kDup = kLPT >> kHalve;          // lanes holding identical values
   static constexpr int kStages = 3;
+  static constexpr int kQueue = 4;                     // work items announced ahead by the producer
+  static constexpr int kQBytes = G * D * (int)sizeof(T);  // query rows of one item (in the queue entry)
+  static constexpr int kEntryBytes = 64 + kQBytes;     // [metadata][q rows]
   static constexpr int kRedFloats = kWarps * G * (D + 2);
   static constexpr int kPFloats = kTile * G;
-  static constexpr int kSmemBytes = 2 * kStages * kTileBytes + 2 * kStages * 8 +
-                                    (kRedFloats + kPFloats) * 4 + 16;
+  // smem: K ring | V ring | item queue | barriers | reductions | probabilities
+  static constexpr int kOffQueue = 2 * kStages * kTileBytes;
+  static constexpr int kOffBars = kOffQueue + kQueue * kEntryBytes;
+  static constexpr int kNumBars = 2 * kStages + 2 * kQueue;
+  static constexpr int kOffRed = kOffBars + kNumBars * 8;
+  static constexpr int kSmemBytes = kOffRed + (kRedFloats + kPFloats) * 4 + 16;
   static_assert(kEPV * kLPT == D, "head_dim must be a multiple of the vector width");
   static_assert(kLPT <= 32 && kTPP * kLPT == 32, "lanes per token must divide 32");
   static_assert(kNP == 8, "tile geometry");
   static_assert(kRV % G == 0, "each lane must keep whole passes");
+  static_assert(kQBytes % 16 == 0 && kEntryBytes % 16 == 0, "queue entries hold 16-byte aligned copies");
 };
 
+// One work item: a split of one (request, KV head) cache.  ntok < 0 ends the stream.
+struct DecodeItem {
+  int b, kvh, split, t0, ntok, nsplit;
+};
+
+// Consumer-warp barrier (named barrier 1, the 4 consumer warps only): every
+// consumer warp reaches each use exactly once per item, also on the abort
+// path, so the producer warp never takes part and never blocks it.
+template <int kWarps>
+__device__ __forceinline__ void consumer_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kWarps * 32) : "memory");
+}
+// Same barrier, returning the OR of every consumer thread's predicate, so that
+// all consumer warps take the same branch after it.
+template <int kWarps>
+__device__ __forceinline__ bool consumer_any(bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, %2, p;\n selp.u32 %0, 1, 0, q;\n}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "n"(kWarps * 32)
+      : "memory");
+  return r != 0;
+}
+
+// Persistent CTAs (as many as fit on the device at once) run through the
+// (request, KV head, split) work items.  With a workspace the items are handed
+// out by an atomic counter (ragged cache lengths make a static split
+// uneven), else round-robin.  The producer warp claims items, announces each
+// one in a small shared-memory queue (metadata and the item's query rows,
+// copied by TMA), and streams its K/V tiles into a ring that runs on across
+// items, so the copies for the next item are in flight while the consumers
+// finish the current one.
 template <typename T, int D, int G>
 __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kThreads)
     decode_gqa_kernel(const DecodeArgs a) {
@@ -61,27 +103,22 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kThreads)
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* sk = smem;
   uint8_t* sv = smem + C::kStages * C::kTileBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * C::kStages * C::kTileBytes);
-  float* red = reinterpret_cast<float*>(bars + 2 * C::kStages);  // [warp][G][D+2]
-  float* ps = red + C::kRedFloats;                                // [tile token][G]
+  uint8_t* queue = smem + C::kOffQueue;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBars);
+  float* red = reinterpret_cast<float*>(smem + C::kOffRed);  // [warp][G][D+2]
+  float* ps = red + C::kRedFloats;                             // [tile token][G]
   __shared__ int s_abort;
   __shared__ int s_last;
-
-  const int split = blockIdx.x;
-  const int kvh = blockIdx.y;
-  const int b = blockIdx.z;
-  int len = a.cap;
-  if (a.kv_lens != nullptr) len = min(max(a.kv_lens[b], 0), a.cap);
-  const int nsplit = max(1, (len + a.split_tokens - 1) / a.split_tokens);
-  if (split >= nsplit) return;  // uniform for the CTA
-  const int t0 = split * a.split_tokens;
-  const int ntok = max(0, min(len, t0 + a.split_tokens) - t0);
-  const int ntiles = (ntok + C::kTile - 1) / C::kTile;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t full0 = smem_u32(bars);
   const uint32_t empty0 = smem_u32(bars + C::kStages);
+  const uint32_t qfull0 = smem_u32(bars + 2 * C::kStages);
+  const uint32_t qempty0 = smem_u32(bars + 2 * C::kStages + C::kQueue);
+  const int total_items = a.batch * a.hkv * a.max_splits;
+  const bool dynamic = a.ws_count != nullptr;
+  unsigned int* next_item = dynamic ? a.ws_sched : nullptr;
 
   if (threadIdx.x == 0) {
     s_abort = 0;
@@ -89,37 +126,99 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kThreads)
       mbar_init(full0 + 8 * s, 1);
       mbar_init(empty0 + 8 * s, C::kWarps);
     }
+    for (int i = 0; i < C::kQueue; ++i) {
+      mbar_init(qfull0 + 8 * i, 1);
+      mbar_init(qempty0 + 8 * i, C::kWarps);
+    }
     fence_mbar_init();
   }
   __syncthreads();
-
-  const uint8_t* gk = static_cast<const uint8_t*>(a.k) +
-                      ((int64_t)b * a.k_sb + (int64_t)kvh * a.k_sh + (int64_t)t0 * D) * sizeof(T);
-  const uint8_t* gv = static_cast<const uint8_t*>(a.v) +
-                      ((int64_t)b * a.v_sb + (int64_t)kvh * a.v_sh + (int64_t)t0 * D) * sizeof(T);
-
-  float o[G][C::kEPV];
-  float m[G], l[G];
 
   if (warp == C::kWarps) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       const uint64_t pol = l2_policy_evict_first();
-      int issued = 0;
-      for (int t = 0; t < ntiles; ++t) {
-        const int s = t % C::kStages;
-        const int u = t / C::kStages;
-        if (t >= C::kStages && !mbar_wait(empty0 + 8 * s, (u - 1) & 1, &s_abort, a.err)) break;
-        const uint32_t nb = (uint32_t)min(C::kTile, ntok - t * C::kTile) * C::kRowBytes;
-        mbar_arrive_expect_tx(full0 + 8 * s, 2 * nb);
-        bulk_g2s(smem_u32(sk + s * C::kTileBytes), gk + (int64_t)t * C::kTileBytes, nb, full0 + 8 * s, pol);
-        bulk_g2s(smem_u32(sv + s * C::kTileBytes), gv + (int64_t)t * C::kTileBytes, nb, full0 + 8 * s, pol);
-        ++issued;
+      uint32_t g = 0;       // K/V tiles issued so far (ring position)
+      uint32_t qi = 0;      // items announced so far (queue position)
+      int k = 0;            // round-robin position (static scheduling)
+      bool ok = true;
+      for (;;) {
+        // claim the next non-empty item (or run out)
+        int item = -1;
+        DecodeItem it;
+        for (;;) {
+          int cand;
+          if (dynamic) {
+            cand = (int)atomicAdd(next_item, 1u);
+          } else {
+            cand = (int)blockIdx.x + k * (int)gridDim.x;
+            ++k;
+          }
+          if (cand >= total_items) break;
+          // split-major order: item = split * (B * Hkv) + (b * Hkv + kvh)
+          const int bh = cand % (a.batch * a.hkv);
+          it.split = cand / (a.batch * a.hkv);
+          it.b = bh / a.hkv;
+          it.kvh = bh % a.hkv;
+          int len = a.cap;
+          if (a.kv_lens != nullptr) len = min(max(__ldg(a.kv_lens + it.b), 0), a.cap);
+          it.nsplit = max(1, (len + a.split_tokens - 1) / a.split_tokens);
+          if (it.split >= it.nsplit) continue;  // past this request's length
+          it.t0 = it.split * a.split_tokens;
+          it.ntok = max(0, min(len, it.t0 + a.split_tokens) - it.t0);
+          item = cand;
+          break;
+        }
+        // announce it (or the end of the stream)
+        const uint32_t slot = qi % C::kQueue;
+        if (qi >= (uint32_t)C::kQueue && !mbar_wait(qempty0 + 8 * slot, (qi / C::kQueue - 1) & 1, &s_abort, a.err)) {
+          ok = false;
+          break;
+        }
+        DecodeItem* meta = reinterpret_cast<DecodeItem*>(queue + slot * C::kEntryBytes);
+        if (item < 0) {
+          meta->ntok = -1;
+          mbar_arrive(qfull0 + 8 * slot);  // release: the consumers see the end marker
+          ++qi;
+          break;
+        }
+        *meta = it;
+        const T* qsrc = static_cast<const T*>(a.q) + (int64_t)it.b * a.q_sb + (int64_t)(it.kvh * G) * a.q_sh;
+        const uint32_t qdst = smem_u32(queue + slot * C::kEntryBytes + 64);
+        mbar_arrive_expect_tx(qfull0 + 8 * slot, C::kQBytes);  // also publishes the metadata (release)
+        if (a.q_sh == D) {
+          bulk_g2s(qdst, qsrc, C::kQBytes, qfull0 + 8 * slot, pol);
+        } else {
+          for (int h = 0; h < G; ++h)
+            bulk_g2s(qdst + h * C::kRowBytes, qsrc + (int64_t)h * a.q_sh, C::kRowBytes, qfull0 + 8 * slot, pol);
+        }
+        ++qi;
+        // its K/V tiles
+        const uint8_t* gk = static_cast<const uint8_t*>(a.k) +
+                            ((int64_t)it.b * a.k_sb + (int64_t)it.kvh * a.k_sh + (int64_t)it.t0 * D) * sizeof(T);
+        const uint8_t* gv = static_cast<const uint8_t*>(a.v) +
+                            ((int64_t)it.b * a.v_sb + (int64_t)it.kvh * a.v_sh + (int64_t)it.t0 * D) * sizeof(T);
+        const int ntiles = (it.ntok + C::kTile - 1) / C::kTile;
+        for (int t = 0; t < ntiles; ++t, ++g) {
+          const uint32_t s = g % C::kStages, u = g / C::kStages;
+          if (u > 0 && !mbar_wait(empty0 + 8 * s, (u - 1) & 1, &s_abort, a.err)) {
+            ok = false;
+            break;
+          }
+          const uint32_t nb = (uint32_t)min(C::kTile, it.ntok - t * C::kTile) * C::kRowBytes;
+          mbar_arrive_expect_tx(full0 + 8 * s, 2 * nb);
+          bulk_g2s(smem_u32(sk + s * C::kTileBytes), gk + (int64_t)t * C::kTileBytes, nb, full0 + 8 * s, pol);
+          bulk_g2s(smem_u32(sv + s * C::kTileBytes), gv + (int64_t)t * C::kTileBytes, nb, full0 + 8 * s, pol);
+        }
+        if (!ok) break;
       }
-      if (s_abort) {
+      if (!ok || s_abort) {
         // do not leave while our own copies may still land in shared memory
-        for (int t = max(0, issued - C::kStages); t < issued; ++t)
+        for (uint32_t t = g > (uint32_t)C::kStages ? g - C::kStages : 0u; t < g; ++t)
           mbar_wait(full0 + 8 * (t % C::kStages), (t / C::kStages) & 1, nullptr, a.err);
+        for (uint32_t i = qi > (uint32_t)C::kQueue ? qi - C::kQueue : 0u; i < qi; ++i)
+          mbar_wait(qfull0 + 8 * (i % C::kQueue), (i / C::kQueue) & 1, nullptr, a.err);
+        s_abort = 1;
       }
     }
   } else {
@@ -127,19 +226,6 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kThreads)
     const int c = lane % C::kLPT;    // 16-byte column of the head_dim row
     const int sub = lane / C::kLPT;  // token slot within a pass
     const int gl = c;                // lane index inside its token group
-    float qf[G][C::kEPV];
-#pragma unroll
-    for (int h = 0; h < G; ++h) {
-      const T* qp = static_cast<const T*>(a.q) + (int64_t)b * a.q_sb + (int64_t)(kvh * G + h) * a.q_sh;
-      const uint4 u = *reinterpret_cast<const uint4*>(qp + c * C::kEPV);
-      Elem<T>::unpack(u, qf[h]);
-#pragma unroll
-      for (int e = 0; e < C::kEPV; ++e) qf[h][e] *= a.scale_log2;
-      m[h] = -INFINITY;
-      l[h] = 0.f;
-#pragma unroll
-      for (int e = 0; e < C::kEPV; ++e) o[h][e] = 0.f;
-    }
     // index of the first value this lane keeps after the reduce-scatter
     int idx_base = 0;
 #pragma unroll
@@ -147,237 +233,295 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kThreads)
       if (gl & (C::kLPT >> (k + 1))) idx_base += C::kNV >> (k + 1);
     const bool canonical = (gl % C::kDup) == 0;
     float* pw = ps + warp * C::kTPW * G;  // this warp's probabilities [token][G]
-
-    for (int t = 0; t < ntiles; ++t) {
-      const int s = t % C::kStages;
-      if (!mbar_wait(full0 + 8 * s, (t / C::kStages) & 1, &s_abort, a.err)) break;
-      const uint8_t* tk = sk + s * C::kTileBytes;
-      const uint8_t* tv = sv + s * C::kTileBytes;
-      const int nvalid = min(C::kTile, ntok - t * C::kTile);
-      const int wtok0 = warp * C::kTPW;  // first tile token of this warp
-
-      // ---- scores: partial dot products over this lane's 16-byte column
-      float sc[C::kNV];
-#pragma unroll
-      for (int p = 0; p < C::kNP; ++p) {
-        const int tok = wtok0 + p * C::kTPP + sub;
-        const uint4 u = *reinterpret_cast<const uint4*>(tk + tok * C::kRowBytes + c * 16);
-        float kf[C::kEPV];
-        Elem<T>::unpack(u, kf);
-#pragma unroll
-        for (int h = 0; h < G; ++h) {
-          float acc = 0.f;
-#pragma unroll
-          for (int e = 0; e < C::kEPV; ++e) acc = fmaf(qf[h][e], kf[e], acc);
-          sc[p * G + h] = acc;
-        }
-      }
-      // ---- reduce-scatter across the kLPT lanes of a token, then butterfly
-#pragma unroll
-      for (int k = 0; k < C::kHalve; ++k) {
-        const int off = C::kLPT >> (k + 1);
-        const int half = C::kNV >> (k + 1);
-        const bool upper = (gl & off) != 0;
-#pragma unroll
-        for (int i = 0; i < half; ++i) {
-          const float send = upper ? sc[i] : sc[i + half];
-          const float keep = upper ? sc[i + half] : sc[i];
-          sc[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
-        }
-      }
-#pragma unroll
-      for (int k = C::kHalve; k < C::kLogLPT; ++k) {
-        const int off = C::kLPT >> (k + 1);
-#pragma unroll
-        for (int i = 0; i < C::kRV; ++i) sc[i] += __shfl_xor_sync(0xffffffffu, sc[i], off);
-      }
-      // lane now holds values idx_base .. idx_base + kRV - 1, i.e. passes
-      // idx_base/G .. + kRV/G - 1 for every head; mask tokens past the split end
-#pragma unroll
-      for (int r = 0; r < C::kRV; ++r) {
-        const int pass = (idx_base + r) / G;
-        const int tok = wtok0 + pass * C::kTPP + sub;
-        if (tok >= nvalid) sc[r] = -INFINITY;
-      }
-      // ---- online softmax, one state per warp and head
+    uint32_t g = 0;                       // ring position
+    for (uint32_t qi = 0;; ++qi) {
+      // ---- next item from the queue (every consumer warp takes every item)
+      const uint32_t slot = qi % C::kQueue;
+      const bool got = mbar_wait(qfull0 + 8 * slot, (qi / C::kQueue) & 1, &s_abort, a.err);
+      const DecodeItem it = *reinterpret_cast<const DecodeItem*>(queue + slot * C::kEntryBytes);
+      // every consumer warp leaves at the same item (the named barriers below
+      // need all four): the stop decision is OR-reduced over them
+      if (consumer_any<C::kWarps>(!got || it.ntok < 0 || s_abort != 0)) break;
+      float qf[G][C::kEPV];
+      float o[G][C::kEPV];
+      float m[G], l[G];
 #pragma unroll
       for (int h = 0; h < G; ++h) {
-        float mt = -INFINITY;
+        const uint4 u = *reinterpret_cast<const uint4*>(queue + slot * C::kEntryBytes + 64 + h * C::kRowBytes + c * 16);
+        Elem<T>::unpack(u, qf[h]);
 #pragma unroll
-        for (int r = h; r < C::kRV; r += G) mt = fmaxf(mt, sc[r]);
+        for (int e = 0; e < C::kEPV; ++e) qf[h][e] *= a.scale_log2;
+        m[h] = -INFINITY;
+        l[h] = 0.f;
 #pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, off));
-        const float m_new = fmaxf(m[h], mt);
-        const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-        if (m_new != m[h]) {
-          const float alpha = exp2f(m[h] - m_use);
-          l[h] *= alpha;
-#pragma unroll
-          for (int e = 0; e < C::kEPV; ++e) o[h][e] *= alpha;
-          m[h] = m_new;
-        }
-        float lsum = 0.f;
-#pragma unroll
-        for (int r = h; r < C::kRV; r += G) {
-          const float p = exp2f(sc[r] - m_use);
-          lsum += p;
-          if (canonical) {
-            const int pass = (idx_base + r) / G;
-            pw[(pass * C::kTPP + sub) * G + h] = p;
-          }
-        }
-        if (canonical) l[h] += lsum;
+        for (int e = 0; e < C::kEPV; ++e) o[h][e] = 0.f;
       }
       __syncwarp();
-      // ---- o += P V over this lane's column (P rounded to the cache dtype)
+      if (lane == 0) mbar_arrive(qempty0 + 8 * slot);  // entry read: the producer may reuse it
+      const int ntiles = (it.ntok + C::kTile - 1) / C::kTile;
+      for (int t = 0; t < ntiles; ++t, ++g) {
+        const uint32_t s = g % C::kStages;
+        if (!mbar_wait(full0 + 8 * s, (g / C::kStages) & 1, &s_abort, a.err)) {
+          g += ntiles - t;  // keep the ring position consistent (the kernel is ending anyway)
+          break;
+        }
+        const uint8_t* tk = sk + s * C::kTileBytes;
+        const uint8_t* tv = sv + s * C::kTileBytes;
+        const int nvalid = min(C::kTile, it.ntok - t * C::kTile);
+        const int wtok0 = warp * C::kTPW;  // first tile token of this warp
+
+        // ---- scores: partial dot products over this lane's 16-byte column
+        float sc[C::kNV];
 #pragma unroll
-      for (int p = 0; p < C::kNP; ++p) {
-        const int wt = p * C::kTPP + sub;
-        if (wtok0 + wt < nvalid) {
-          const uint4 u = *reinterpret_cast<const uint4*>(tv + (wtok0 + wt) * C::kRowBytes + c * 16);
-          float vf[C::kEPV];
-          Elem<T>::unpack(u, vf);
+        for (int p = 0; p < C::kNP; ++p) {
+          const int tok = wtok0 + p * C::kTPP + sub;
+          const uint4 u = *reinterpret_cast<const uint4*>(tk + tok * C::kRowBytes + c * 16);
+          float kf[C::kEPV];
+          Elem<T>::unpack(u, kf);
 #pragma unroll
           for (int h = 0; h < G; ++h) {
-            const float pr = Elem<T>::to_float(Elem<T>::from_float(pw[wt * G + h]));
+            float acc = 0.f;
 #pragma unroll
-            for (int e = 0; e < C::kEPV; ++e) o[h][e] = fmaf(pr, vf[e], o[h][e]);
+            for (int e = 0; e < C::kEPV; ++e) acc = fmaf(qf[h][e], kf[e], acc);
+            sc[p * G + h] = acc;
           }
         }
+        // ---- reduce-scatter across the kLPT lanes of a token, then butterfly
+#pragma unroll
+        for (int k = 0; k < C::kHalve; ++k) {
+          const int off = C::kLPT >> (k + 1);
+          const int half = C::kNV >> (k + 1);
+          const bool upper = (gl & off) != 0;
+#pragma unroll
+          for (int i = 0; i < half; ++i) {
+            const float send = upper ? sc[i] : sc[i + half];
+            const float keep = upper ? sc[i + half] : sc[i];
+            sc[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+          }
+        }
+#pragma unroll
+        for (int k = C::kHalve; k < C::kLogLPT; ++k) {
+          const int off = C::kLPT >> (k + 1);
+#pragma unroll
+          for (int i = 0; i < C::kRV; ++i) sc[i] += __shfl_xor_sync(0xffffffffu, sc[i], off);
+        }
+        // lane now holds values idx_base .. idx_base + kRV - 1, i.e. passes
+        // idx_base/G .. + kRV/G - 1 for every head; mask tokens past the split end
+#pragma unroll
+        for (int r = 0; r < C::kRV; ++r) {
+          const int pass = (idx_base + r) / G;
+          const int tok = wtok0 + pass * C::kTPP + sub;
+          if (tok >= nvalid) sc[r] = -INFINITY;
+        }
+        // ---- online softmax, one state per warp and head
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+          float mt = -INFINITY;
+#pragma unroll
+          for (int r = h; r < C::kRV; r += G) mt = fmaxf(mt, sc[r]);
+#pragma unroll
+          for (int off = 16; off >= 1; off >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, off));
+          const float m_new = fmaxf(m[h], mt);
+          const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+          if (m_new != m[h]) {
+            const float alpha = exp2f(m[h] - m_use);
+            l[h] *= alpha;
+#pragma unroll
+            for (int e = 0; e < C::kEPV; ++e) o[h][e] *= alpha;
+            m[h] = m_new;
+          }
+          float lsum = 0.f;
+#pragma unroll
+          for (int r = h; r < C::kRV; r += G) {
+            const float p = exp2f(sc[r] - m_use);
+            lsum += p;
+            if (canonical) {
+              const int pass = (idx_base + r) / G;
+              pw[(pass * C::kTPP + sub) * G + h] = p;
+            }
+          }
+          if (canonical) l[h] += lsum;
+        }
+        __syncwarp();
+        // ---- o += P V over this lane's column (P rounded to the cache dtype)
+#pragma unroll
+        for (int p = 0; p < C::kNP; ++p) {
+          const int wt = p * C::kTPP + sub;
+          if (wtok0 + wt < nvalid) {
+            const uint4 u = *reinterpret_cast<const uint4*>(tv + (wtok0 + wt) * C::kRowBytes + c * 16);
+            float vf[C::kEPV];
+            Elem<T>::unpack(u, vf);
+#pragma unroll
+            for (int h = 0; h < G; ++h) {
+              const float pr = Elem<T>::to_float(Elem<T>::from_float(pw[wt * G + h]));
+#pragma unroll
+              for (int e = 0; e < C::kEPV; ++e) o[h][e] = fmaf(pr, vf[e], o[h][e]);
+            }
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty0 + 8 * s);
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(empty0 + 8 * s);
-    }
 
-    // ---- combine the token slots of the warp, then publish per-warp state
+      // ---- combine the token slots of the warp, then publish per-warp state
 #pragma unroll
-    for (int h = 0; h < G; ++h) {
+      for (int h = 0; h < G; ++h) {
 #pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) l[h] += __shfl_xor_sync(0xffffffffu, l[h], off);
+        for (int off = 16; off >= 1; off >>= 1) l[h] += __shfl_xor_sync(0xffffffffu, l[h], off);
 #pragma unroll
-      for (int off = C::kLPT; off < 32; off <<= 1) {
+        for (int off = C::kLPT; off < 32; off <<= 1) {
 #pragma unroll
-        for (int e = 0; e < C::kEPV; ++e) o[h][e] += __shfl_xor_sync(0xffffffffu, o[h][e], off);
+          for (int e = 0; e < C::kEPV; ++e) o[h][e] += __shfl_xor_sync(0xffffffffu, o[h][e], off);
+        }
+        float* rw = red + (warp * G + h) * (D + 2);
+        if (sub == 0) {
+#pragma unroll
+          for (int e = 0; e < C::kEPV; ++e) rw[c * C::kEPV + e] = o[h][e];
+        }
+        if (lane == 0) {
+          rw[D] = m[h];
+          rw[D + 1] = l[h];
+        }
       }
-      float* rw = red + (warp * G + h) * (D + 2);
-      if (sub == 0) {
-#pragma unroll
-        for (int e = 0; e < C::kEPV; ++e) rw[c * C::kEPV + e] = o[h][e];
-      }
-      if (lane == 0) {
-        rw[D] = m[h];
-        rw[D + 1] = l[h];
-      }
-    }
-  }
-  __syncthreads();
+      consumer_sync<C::kWarps>();
 
-  // ---- merge the consumer warps: result for (h, d) of this split
-  const int bh = b * a.hkv + kvh;
-  const bool single = (nsplit == 1);
-  for (int idx = threadIdx.x; idx < G * D; idx += C::kThreads) {
-    const int h = idx / D, d = idx % D;
-    float M = -INFINITY;
+      // ---- merge the consumer warps: result for (h, d) of this split
+      const int bh = it.b * a.hkv + it.kvh;
+      const bool single = (it.nsplit == 1);
+      for (int idx = threadIdx.x; idx < G * D; idx += C::kWarps * 32) {
+        const int h = idx / D, d = idx % D;
+        float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < C::kWarps; ++w) M = fmaxf(M, red[(w * G + h) * (D + 2) + D]);
-    float L = 0.f, O = 0.f;
-    if (M != -INFINITY) {
+        for (int w = 0; w < C::kWarps; ++w) M = fmaxf(M, red[(w * G + h) * (D + 2) + D]);
+        float L = 0.f, O = 0.f;
+        if (M != -INFINITY) {
 #pragma unroll
-      for (int w = 0; w < C::kWarps; ++w) {
-        const float* rw = red + (w * G + h) * (D + 2);
-        const float sc = exp2f(rw[D] - M);
-        L += rw[D + 1] * sc;
-        O += rw[d] * sc;
+          for (int w = 0; w < C::kWarps; ++w) {
+            const float* rw = red + (w * G + h) * (D + 2);
+            const float sc = exp2f(rw[D] - M);
+            L += rw[D + 1] * sc;
+            O += rw[d] * sc;
+          }
+        }
+        const float ov = (L > 0.f) ? O / L : 0.f;
+        const float lse = (L > 0.f) ? M + log2f(L) : -INFINITY;
+        const int qh = it.kvh * G + h;
+        if (single) {
+          if (a.out != nullptr)
+            static_cast<T*>(a.out)[(int64_t)it.b * a.o_sb + (int64_t)qh * a.o_sh + d] = Elem<T>::from_float(ov);
+          if (a.partial_o != nullptr) a.partial_o[((int64_t)it.b * a.hq + qh) * D + d] = ov;
+          if (a.lse != nullptr && d == 0) a.lse[(int64_t)it.b * a.hq + qh] = lse;
+        } else {
+          a.ws_o[(((int64_t)bh * a.max_splits + it.split) * G + h) * D + d] = ov;
+          if (d == 0) a.ws_lse[((int64_t)bh * a.max_splits + it.split) * G + h] = lse;
+        }
       }
-    }
-    const float ov = (L > 0.f) ? O / L : 0.f;
-    const float lse = (L > 0.f) ? M + log2f(L) : -INFINITY;
-    const int qh = kvh * G + h;
-    if (single) {
-      if (a.out != nullptr)
-        static_cast<T*>(a.out)[(int64_t)b * a.o_sb + (int64_t)qh * a.o_sh + d] = Elem<T>::from_float(ov);
-      if (a.partial_o != nullptr) a.partial_o[((int64_t)b * a.hq + qh) * D + d] = ov;
-      if (a.lse != nullptr && d == 0) a.lse[(int64_t)b * a.hq + qh] = lse;
-    } else {
-      a.ws_o[(((int64_t)bh * a.max_splits + split) * G + h) * D + d] = ov;
-      if (d == 0) a.ws_lse[((int64_t)bh * a.max_splits + split) * G + h] = lse;
+      if (!single) {
+        // ---- split-KV: the last split of this (request, KV head) to finish merges all of them
+        __threadfence();
+        consumer_sync<C::kWarps>();
+        if (threadIdx.x == 0) {
+          const unsigned int prev = atomicAdd(&a.ws_count[bh], 1u);
+          s_last = (prev == (unsigned int)(it.nsplit - 1));
+          if (s_last) __threadfence();
+        }
+        consumer_sync<C::kWarps>();
+        if (s_last) {
+          for (int idx = threadIdx.x; idx < G * D; idx += C::kWarps * 32) {
+            const int h = idx / D, d = idx % D;
+            float M = -INFINITY;
+            for (int sp = 0; sp < it.nsplit; ++sp)
+              M = fmaxf(M, __ldcg(a.ws_lse + ((int64_t)bh * a.max_splits + sp) * G + h));
+            float L = 0.f, O = 0.f;
+            if (M != -INFINITY) {
+              for (int sp = 0; sp < it.nsplit; ++sp) {
+                const int64_t base = ((int64_t)bh * a.max_splits + sp) * G + h;
+                const float w = exp2f(__ldcg(a.ws_lse + base) - M);
+                L += w;
+                O += w * __ldcg(a.ws_o + base * D + d);
+              }
+            }
+            const float ov = (L > 0.f) ? O / L : 0.f;
+            const float lse = (L > 0.f) ? M + log2f(L) : -INFINITY;
+            const int qh = it.kvh * G + h;
+            if (a.out != nullptr)
+              static_cast<T*>(a.out)[(int64_t)it.b * a.o_sb + (int64_t)qh * a.o_sh + d] = Elem<T>::from_float(ov);
+            if (a.partial_o != nullptr) a.partial_o[((int64_t)it.b * a.hq + qh) * D + d] = ov;
+            if (a.lse != nullptr && d == 0) a.lse[(int64_t)it.b * a.hq + qh] = lse;
+          }
+          if (threadIdx.x == 0) a.ws_count[bh] = 0u;  // ready for the next call
+        }
+      }
+      // the reductions buffer and s_last are reused by the next item
+      consumer_sync<C::kWarps>();
     }
   }
-  if (single) return;
 
-  // ---- split-KV: the last CTA of this (request, KV head) merges all splits
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const unsigned int prev = atomicAdd(&a.ws_count[bh], 1u);
-    s_last = (prev == (unsigned int)(nsplit - 1));
-    if (s_last) __threadfence();
-  }
-  __syncthreads();
-  if (!s_last) return;
-  for (int idx = threadIdx.x; idx < G * D; idx += C::kThreads) {
-    const int h = idx / D, d = idx % D;
-    float M = -INFINITY;
-    for (int s = 0; s < nsplit; ++s)
-      M = fmaxf(M, __ldcg(a.ws_lse + ((int64_t)bh * a.max_splits + s) * G + h));
-    float L = 0.f, O = 0.f;
-    if (M != -INFINITY) {
-      for (int s = 0; s < nsplit; ++s) {
-        const int64_t base = ((int64_t)bh * a.max_splits + s) * G + h;
-        const float w = exp2f(__ldcg(a.ws_lse + base) - M);
-        L += w;
-        O += w * __ldcg(a.ws_o + base * D + d);
+  // ---- scheduling counters back to zero for the next call: the last CTA out resets them
+  if (dynamic) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      const unsigned int done = atomicAdd(a.ws_sched + 1, 1u);
+      if (done == gridDim.x - 1) {
+        a.ws_sched[0] = 0u;
+        a.ws_sched[1] = 0u;
+        __threadfence();
       }
     }
-    const float ov = (L > 0.f) ? O / L : 0.f;
-    const float lse = (L > 0.f) ? M + log2f(L) : -INFINITY;
-    const int qh = kvh * G + h;
-    if (a.out != nullptr)
-      static_cast<T*>(a.out)[(int64_t)b * a.o_sb + (int64_t)qh * a.o_sh + d] = Elem<T>::from_float(ov);
-    if (a.partial_o != nullptr) a.partial_o[((int64_t)b * a.hq + qh) * D + d] = ov;
-    if (a.lse != nullptr && d == 0) a.lse[(int64_t)b * a.hq + qh] = lse;
   }
-  if (threadIdx.x == 0) a.ws_count[bh] = 0u;  // ready for the next call
 }
 
 // ------------------------------------------------------------------ host side
 
 template <typename T, int D, int G>
-static cudaError_t launch_decode_t(const DecodeArgs& a, dim3 grid, cudaStream_t st) {
+static cudaError_t launch_decode_t(const DecodeArgs& a, cudaStream_t st) {
   using C = DecodeCfg<T, D, G>;
-  // the dynamic shared-memory opt-in is per function and per device
-  static bool attr_set[64] = {false};
+  // the dynamic shared-memory opt-in and the co-resident CTA count are per
+  // function and per device
+  static int resident[64] = {0};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+  int per_device = (dev >= 0 && dev < 64) ? resident[dev] : 0;
+  if (per_device == 0) {
     e = cudaFuncSetAttribute(decode_gqa_kernel<T, D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              C::kSmemBytes);
     if (e != cudaSuccess) return e;
-    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    int per_sm = 0, sms = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_gqa_kernel<T, D, G>, C::kThreads,
+                                                      C::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    per_device = per_sm * sms;
+    if (per_device <= 0) return cudaErrorInvalidConfiguration;
+    if (dev >= 0 && dev < 64) resident[dev] = per_device;
   }
+  const long long items = (long long)a.batch * a.hkv * a.max_splits;
+  const int grid = (int)(items < per_device ? items : per_device);
   decode_gqa_kernel<T, D, G><<<grid, C::kThreads, C::kSmemBytes, st>>>(a);
   return cudaGetLastError();
 }
 
 template <typename T, int D>
-static cudaError_t dispatch_g(int g, const DecodeArgs& a, dim3 grid, cudaStream_t st) {
+static cudaError_t dispatch_g(int g, const DecodeArgs& a, cudaStream_t st) {
   switch (g) {
-    case 1: return launch_decode_t<T, D, 1>(a, grid, st);
-    case 2: return launch_decode_t<T, D, 2>(a, grid, st);
-    case 4: return launch_decode_t<T, D, 4>(a, grid, st);
-    case 8: return launch_decode_t<T, D, 8>(a, grid, st);
+    case 1: return launch_decode_t<T, D, 1>(a, st);
+    case 2: return launch_decode_t<T, D, 2>(a, st);
+    case 4: return launch_decode_t<T, D, 4>(a, st);
+    case 8: return launch_decode_t<T, D, 8>(a, st);
   }
   return cudaErrorInvalidValue;
 }
 
 template <typename T>
-static cudaError_t dispatch_d(int d, int g, const DecodeArgs& a, dim3 grid, cudaStream_t st) {
+static cudaError_t dispatch_d(int d, int g, const DecodeArgs& a, cudaStream_t st) {
   switch (d) {
-    case 16: return dispatch_g<T, 16>(g, a, grid, st);
-    case 32: return dispatch_g<T, 32>(g, a, grid, st);
-    case 64: return dispatch_g<T, 64>(g, a, grid, st);
-    case 128: return dispatch_g<T, 128>(g, a, grid, st);
+    case 16: return dispatch_g<T, 16>(g, a, st);
+    case 32: return dispatch_g<T, 32>(g, a, st);
+    case 64: return dispatch_g<T, 64>(g, a, st);
+    case 128: return dispatch_g<T, 128>(g, a, st);
   }
   return cudaErrorInvalidValue;
 }
@@ -389,11 +533,10 @@ int decode_tile_for(int dtype, int head_dim) {
 }
 
 cudaError_t launch_decode(int dtype, int head_dim, int group, const DecodeArgs& a, cudaStream_t st) {
-  dim3 grid(a.max_splits, a.hkv, a.batch);
   switch (dtype) {
-    case AICAS_DTYPE_F32: return dispatch_d<float>(head_dim, group, a, grid, st);
-    case AICAS_DTYPE_F16: return dispatch_d<__half>(head_dim, group, a, grid, st);
-    case AICAS_DTYPE_BF16: return dispatch_d<__nv_bfloat16>(head_dim, group, a, grid, st);
+    case AICAS_DTYPE_F32: return dispatch_d<float>(head_dim, group, a, st);
+    case AICAS_DTYPE_F16: return dispatch_d<__half>(head_dim, group, a, st);
+    case AICAS_DTYPE_BF16: return dispatch_d<__nv_bfloat16>(head_dim, group, a, st);
   }
   return cudaErrorInvalidValue;
 }

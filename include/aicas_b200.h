@@ -69,6 +69,7 @@ extern "C" {
 /* bits of the device-side error word (see aicas_device_error_flags) */
 #define AICAS_DEVERR_WAIT_TIMEOUT 1u /* a bounded barrier wait gave up */
 #define AICAS_DEVERR_TMEM 2u         /* tensor-memory allocation returned an unusable address */
+#define AICAS_DEVERR_PEER_TIMEOUT 4u /* a peer rank did not publish its partial in time */
 
 /* ------------------------------------------------------------------------ */
 /* GQA decode: one query token per request against that request's KV cache. */
@@ -137,6 +138,45 @@ typedef struct aicas_merge_params {
 } aicas_merge_params;
 
 AICAS_API int aicas_merge_partials(const aicas_merge_params* p, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Cross-GPU merge of sequence-sharded decode partials over NVLink peer      */
+/* memory.  No reference counterpart (the reference is single-device); it    */
+/* replaces an all-gather of the partials followed by aicas_merge_partials.  */
+/*                                                                          */
+/* Set-up (once per process group, not on the hot path): every rank          */
+/* allocates an exchange buffer of aicas_exchange_buffer_bytes() with         */
+/* aicas_peer_buffer_alloc (the only entry points that allocate), shares the  */
+/* 64-byte IPC handle with the other ranks, and maps theirs with              */
+/* aicas_peer_buffer_open.  Each aicas_exchange_merge call is collective: all */
+/* ranks make the same sequence of calls with the same sizes.  A rank waits   */
+/* at most a few seconds for the others, then sets AICAS_DEVERR_PEER_TIMEOUT, */
+/* writes zeros and returns; the buffers are then out of step and must be     */
+/* re-created.                                                               */
+/* ------------------------------------------------------------------------ */
+#define AICAS_MAX_EXCHANGE_RANKS 8
+#define AICAS_IPC_HANDLE_BYTES 64
+
+AICAS_API size_t aicas_exchange_buffer_bytes(int32_t world, int32_t batch, int32_t num_heads, int32_t head_dim);
+/* cudaMalloc'd, zeroed buffer of `bytes` on the current device and its IPC handle. */
+AICAS_API int aicas_peer_buffer_alloc(size_t bytes, void** ptr, void* ipc_handle);
+AICAS_API int aicas_peer_buffer_free(void* ptr);
+/* Maps another rank's buffer (its IPC handle) into the current device. */
+AICAS_API int aicas_peer_buffer_open(const void* ipc_handle, void** ptr);
+AICAS_API int aicas_peer_buffer_close(void* ptr);
+
+typedef struct aicas_exchange_params {
+  void* peers[AICAS_MAX_EXCHANGE_RANKS]; /* rank r's buffer as mapped here (own buffer at [rank]) */
+  const float* partial_o;   /* [B, H, D] fp32 local partial, contiguous */
+  const float* partial_lse; /* [B, H] fp32 base-2 LSE, contiguous */
+  void* out;                /* [B, H, D] (strided) merged output */
+  float* lse;               /* optional [B, H] merged LSE */
+  int64_t o_stride_b, o_stride_h;
+  int32_t world, rank, batch, num_heads, head_dim;
+  int32_t dtype;            /* dtype of out */
+} aicas_exchange_params;
+
+AICAS_API int aicas_exchange_merge(const aicas_exchange_params* p, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* Flash attention on the tensor cores (tcgen05): causal GQA prefill and     */
@@ -210,6 +250,7 @@ AICAS_API const char* aicas_version(void);
 #define AICAS_CAP_PREFILL_TCGEN05 4u
 #define AICAS_CAP_VARLEN_TCGEN05 8u
 #define AICAS_CAP_ROPE_APPEND 16u
+#define AICAS_CAP_PEER_EXCHANGE 32u
 AICAS_API uint32_t aicas_capabilities(void);
 
 /* Message of the last failed call on this thread ("" if none). */

@@ -40,6 +40,7 @@ def test_version_and_capabilities(native_lib):
     assert v.startswith("aicas_b200 ") and "sm_100a" in v
     caps = nat.capabilities()
     assert caps & nat.CAP_DECODE and caps & nat.CAP_MERGE and caps & nat.CAP_ROPE_APPEND
+    assert caps & nat.CAP_PEER_EXCHANGE
 
 
 STRUCTS = {
@@ -47,6 +48,7 @@ STRUCTS = {
     "aicas_merge_params": nat.MergeParams,
     "aicas_fmha_params": nat.FmhaParams,
     "aicas_rope_append_params": nat.RopeAppendParams,
+    "aicas_exchange_params": nat.ExchangeParams,
 }
 
 
@@ -163,3 +165,30 @@ def test_rope_append_validation(native_lib):
 def test_merge_validation(native_lib):
     p = nat.MergeParams()
     assert native_lib.aicas_merge_partials(ctypes.byref(p), None) == nat.ERR_INVALID
+
+
+def test_exchange_buffer_size_and_validation(native_lib):
+    # header + 2 parities x world slots of B*H*(D+1) floats rounded up to 4
+    slot = (4 * 16 * 129 + 3) // 4 * 4
+    assert native_lib.aicas_exchange_buffer_bytes(2, 4, 16, 128) == 512 + 2 * 2 * slot * 4
+    assert native_lib.aicas_exchange_buffer_bytes(8, 4, 16, 128) == 512 + 2 * 8 * slot * 4
+    assert native_lib.aicas_exchange_buffer_bytes(9, 4, 16, 128) == 0  # more ranks than the kernel takes
+    assert native_lib.aicas_exchange_buffer_bytes(2, 0, 16, 128) == 0
+    p = nat.ExchangeParams()
+    p.world, p.rank, p.batch, p.num_heads, p.head_dim, p.dtype = 2, 2, 4, 16, 128, nat.DTYPE_BF16
+    assert native_lib.aicas_exchange_merge(ctypes.byref(p), None) == nat.ERR_INVALID
+    assert "rank 2 of world 2" in nat.last_error()
+    p.rank = 0
+    p.partial_o, p.partial_lse, p.out = 1 << 20, 2 << 20, 3 << 20
+    p.peers[0], p.peers[1] = 4 << 20, None
+    assert native_lib.aicas_exchange_merge(ctypes.byref(p), None) == nat.ERR_INVALID
+    assert "rank 1" in nat.last_error()
+    p.peers[1] = (5 << 20) + 16
+    assert native_lib.aicas_exchange_merge(ctypes.byref(p), None) == nat.ERR_INVALID
+    assert "256-byte aligned" in nat.last_error()
+    p.peers[1] = 5 << 20
+    p.head_dim = 130
+    assert native_lib.aicas_exchange_merge(ctypes.byref(p), None) == nat.ERR_INVALID
+    assert "multiple of 4" in nat.last_error()
+    assert native_lib.aicas_peer_buffer_alloc(0, None, None) == nat.ERR_INVALID
+    assert native_lib.aicas_peer_buffer_open(None, None) == nat.ERR_INVALID
