@@ -417,13 +417,15 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kThreads)
         }
       }
       if (!single) {
-        // ---- split-KV: the last split of this (request, KV head) to finish merges all of them
-        __threadfence();
+        // ---- split-KV: the last split of this (request, KV head) to finish merges all of them.
+        // The consumer barrier orders this CTA's partial writes before thread
+        // 0's acquire-release increment at GPU scope (cumulative), which in
+        // turn orders the other splits' partials before the merge reads them.
         consumer_sync<C::kWarps>();
         if (threadIdx.x == 0) {
-          const unsigned int prev = atomicAdd(&a.ws_count[bh], 1u);
+          unsigned int prev;
+          asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(a.ws_count + bh) : "memory");
           s_last = (prev == (unsigned int)(it.nsplit - 1));
-          if (s_last) __threadfence();
         }
         consumer_sync<C::kWarps>();
         if (s_last) {
