@@ -4,7 +4,9 @@
  *
  * Every entry point takes plain pointers, sizes and element strides, launches
  * on the caller's stream, allocates nothing, never synchronises the device and
- * returns an int status (AICAS_OK on success).  On failure a message is kept in
+ * returns an int status (AICAS_OK on success).  The exceptions are the one-time
+ * set-up calls of the cross-GPU exchange (aicas_peer_buffer_*) and the health
+ * query aicas_device_error_flags.  On failure a message is kept in
  * a thread-local buffer readable through aicas_last_error().
  *
  * The entry points replace these operators of the reference package
@@ -18,6 +20,9 @@
  *                             reference never needed because it has no split-KV;
  *                             it combines partials produced by aicas_decode_gqa
  *                             on several devices (sequence-sharded caches)
+ *   aicas_exchange_merge      no reference counterpart (single-device reference):
+ *                             the same merge, with the partials moved between
+ *                             the GPUs over NVLink peer memory in the same kernel
  *   aicas_prefill_gqa_causal  triton_qwen3vl/gqa_flash_attention.py:193-251
  *                             (_gqa_flash_attention_forward, causal, q_len == kv_len)
  *   aicas_varlen_attention    triton_qwen3vl/varlen_flash_attention.py:271-351
