@@ -14,6 +14,10 @@ numbers below are those of the public Qwen3-VL-2B-Instruct configuration; the
 attention shapes they give are the ones the kernels are built and measured on
 (text: 16 query heads over 8 KV heads at head_dim 128; vision: 16 heads at 64).
 
+A third run generates the same tokens with :class:`GraphGreedyDecoder` (a
+preallocated cache and the decode step replayed from one CUDA graph, driven by
+the fused RoPE + append kernel), the serving path a deployment would use.
+
 What is compared (the tolerances live in the tests that call these helpers):
   * ``token_match``: the fraction of generated positions where the patched and
     the SDPA greedy sequences agree, counted up to their first divergence;
@@ -214,6 +218,28 @@ def token_match(a: torch.Tensor, b: torch.Tensor) -> float:
 
 
 @torch.no_grad()
+def graph_generate(model, inputs: dict, max_new_tokens: int, timed: bool = True) -> GenerateRun:
+    """The same greedy generation with :class:`GraphGreedyDecoder`; TTFT is a
+    one-token run (the prefill)."""
+    from .decode_graph import GraphGreedyDecoder
+
+    dec = GraphGreedyDecoder(model)
+    device = inputs["input_ids"].device
+    ttft = float("nan")
+    if timed:
+        _sync(device)
+        t0 = time.perf_counter()
+        dec.generate(inputs, 1)
+        _sync(device)
+        ttft = time.perf_counter() - t0
+    _sync(device)
+    t0 = time.perf_counter()
+    tokens = dec.generate(inputs, max_new_tokens)
+    _sync(device)
+    return GenerateRun(tokens=tokens, seconds=time.perf_counter() - t0, ttft_seconds=ttft)
+
+
+@torch.no_grad()
 def teacher_forced_gap(model, inputs: dict, tokens: torch.Tensor) -> torch.Tensor:
     """[B, new] gaps: the model's best logit minus its logit for ``tokens``, at
     each generated position, with ``tokens`` fed back as the continuation."""
@@ -250,8 +276,11 @@ def run_check(batch: int = 8, seq_len: int = 2048, max_new_tokens: int = 128, gr
     assert attention_in_use(model) == (VISION_BACKEND_KEY, TEXT_BACKEND_KEY)
     greedy_generate(model, warm, 2, timed=False)
     ours = greedy_generate(model, inputs, max_new_tokens, timed)
+    graph_generate(model, warm, 3, timed=False)
+    graph = graph_generate(model, inputs, max_new_tokens, timed)
     set_attention(model, "sdpa")
     gap = teacher_forced_gap(model, inputs, ours.tokens)
+    gap_graph = teacher_forced_gap(model, inputs, graph.tokens)
     result = {
         "batch": batch,
         "prompt_tokens": seq_len,
@@ -263,6 +292,9 @@ def run_check(batch: int = 8, seq_len: int = 2048, max_new_tokens: int = 128, gr
         "mean_logit_gap": float(gap.mean()),
         "patched": {"tokens_per_s": ours.tokens_per_s, "seconds": ours.seconds, "ttft_s": ours.ttft_seconds},
         "sdpa": {"tokens_per_s": ref.tokens_per_s, "seconds": ref.seconds, "ttft_s": ref.ttft_seconds},
+        "graph_decode": {"tokens_per_s": graph.tokens_per_s, "seconds": graph.seconds, "ttft_s": graph.ttft_seconds,
+                         "token_match_vs_patched": token_match(graph.tokens, ours.tokens),
+                         "max_logit_gap": float(gap_graph.max()), "mean_logit_gap": float(gap_graph.mean())},
     }
     del model
     return result

@@ -5,6 +5,9 @@ weights on SDPA.  The prompt is 2048 tokens holding one 64x100-patch image
 (1600 image tokens), so the patched run goes through all three kernels: the
 varlen vision attention, the causal GQA prefill and the GQA decode.
 
+The same generation also runs through GraphGreedyDecoder (preallocated cache,
+decode step replayed from one CUDA graph) and is held to the same bar.
+
 Tolerance: greedy sequences of a random-init model sit on near-ties, so they
 may part after some tokens; what must hold is that SDPA, fed the patched
 tokens, rates each of them within 0.125 (logit units, bf16 model) of its own
@@ -30,6 +33,11 @@ def test_greedy_generate_patched_against_sdpa(cuda_device, native_lib):
     assert r["max_logit_gap"] <= MAX_GAP, r
     assert r["mean_logit_gap"] <= MEAN_GAP, r
     assert r["token_match"] > 0.0, r  # the first generated token comes from the prefill and must agree
+    # the CUDA-graph decode path (preallocated cache, fused RoPE + append) under the same bar
+    g = r["graph_decode"]
+    assert g["max_logit_gap"] <= MAX_GAP, r
+    assert g["mean_logit_gap"] <= MEAN_GAP, r
+    assert g["token_match_vs_patched"] > 0.0, r
     from aicas_b200 import _native
 
     assert _native.device_error_flags() == 0

@@ -67,7 +67,7 @@ def _worker(rank: int, world: int, port: int, path: str, cases, out_dir: str):
 
 
 @pytest.mark.parametrize("path", ["peer", "nccl"])
-@pytest.mark.parametrize("world", [2])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_split_kv_decode_across_gpus(tmp_path, world, path):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
