@@ -611,21 +611,36 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
     if (ok && n_kv > 0) {
       if (warp_wait(o_full(t), (n_kv - 1) & 1, abort_flag, a.err)) {
         tc::fence_after_sync();
+#pragma unroll
+        for (int cc = 0; cc < D / 32; ++cc) tc::tmem_ld32(tl + col_o + 32 * cc, v + 32 * cc);
+        tc::tmem_wait_ld();
         const float inv = l > 0.f ? 1.f / l : 0.f;
+        // O / l through this warp's 32 rows of the tile's Q buffer (free: every
+        // S product of this tile has completed), 16-byte chunks XOR-swizzled by
+        // row; then each store instruction writes whole rows (kChunks lanes per
+        // row), not one 16-byte piece of 32 different rows
+        constexpr int kChunks = D * 2 / 16;
+        constexpr int kRowsPerStore = 32 / kChunks;
+        uint8_t* stage = gb + Lay::kQ + t * Lay::kQTile + qw * (32 * D * 2);
 #pragma unroll
-        for (int cc = 0; cc < D / 32; ++cc) {
-          tc::tmem_ld32(tl + col_o + 32 * cc, v);
-          tc::tmem_wait_ld();
-          if (row_valid) {
-            uint32_t pk[16];
+        for (int ch = 0; ch < kChunks; ++ch) {
+          uint32_t w[4];
 #pragma unroll
-            for (int i = 0; i < 16; ++i)
-              pk[i] = pack2<T>(__uint_as_float(v[2 * i]) * inv, __uint_as_float(v[2 * i + 1]) * inv);
-            uint4* dst = reinterpret_cast<uint4*>(orow + 32 * cc);
+          for (int i = 0; i < 4; ++i)
+            w[i] = pack2<T>(__uint_as_float(v[8 * ch + 2 * i]) * inv, __uint_as_float(v[8 * ch + 2 * i + 1]) * inv);
+          *reinterpret_cast<uint4*>(stage + lane * (D * 2) + ((ch ^ (lane & (kChunks - 1))) << 4)) =
+              make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        __syncwarp();
+        const int wrow0 = tile_row0 + qw * 32;  // first row of this warp
+        T* obase = static_cast<T*>(a.out) + (int64_t)b * a.o_sb + (int64_t)(t ? head1 : head0) * a.o_sh;
 #pragma unroll
-            for (int q4 = 0; q4 < 4; ++q4)
-              dst[q4] = make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
-          }
+        for (int k = 0; k < kChunks; ++k) {
+          const int rr = k * kRowsPerStore + lane / kChunks;
+          const int ch = lane % kChunks;
+          const uint4 val = *reinterpret_cast<const uint4*>(stage + rr * (D * 2) + ((ch ^ (rr & (kChunks - 1))) << 4));
+          if (wrow0 + rr < q_len)
+            *reinterpret_cast<uint4*>(obase + (int64_t)(q_base + wrow0 + rr) * a.o_ss + ch * 8) = val;
         }
       }
     } else if (ok && row_valid) {
