@@ -182,9 +182,10 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
   constexpr int NS = Lay::kStages;
   constexpr int kBN = Lay::kBN;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
-  // pairs out of every 8 (16 columns) whose exponential runs on the FMA pipe:
-  // about 1/4 at head_dim 128, 3/8 at 64 where the products are shorter
-  constexpr int kPolyPairs = D == 128 ? 2 : 3;
+  // pairs out of every 8 (16 columns) whose exponential runs on the FMA pipe
+  // (measured: 2 at head_dim 128; none at 64, where the FMA pipe is busier
+  // with the softmax's other work than the MUFU unit is with ex2)
+  constexpr int kPolyPairs = D == 128 ? 2 : 0;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t sb = (raw + 1023u) & ~1023u;
