@@ -37,7 +37,9 @@ namespace aicas {
 namespace {
 
 constexpr int kBM = 128;  // query rows per tile (MMA M)
-constexpr int kThreads = 384;  // warpgroup 0: producer, MMA (2 warps idle); warpgroups 1, 2: softmax
+// warpgroup 0: producer, MMA (2 warps idle); one softmax warpgroup per query tile
+template <int KT>
+__host__ __device__ constexpr int threads_for() { return 128 + 128 * KT; }
 
 struct FmhaArgs {
   CUtensorMap tm_q, tm_k, tm_v;  // 4-D, box {64 elements, 128 (Q) or BN (K, V) rows, 1 head, 1 batch}
@@ -63,25 +65,27 @@ struct FmhaArgs {
 // memory), which also frees the shared memory the P tiles would take.
 //   S_t at t*128 (fp32);  head_dim 128: O_t at 256 + t*128;
 //   head_dim 64: P_t at 256 + t*64 (16-bit pairs), O_t at 384 + t*64.
-template <int D>
+template <int D, int KT>
 struct Layout {
   static constexpr int kBN = 128;
   static constexpr bool kPTmem = D == 64;
   static constexpr uint32_t kQTile = kBM * D * 2;
   static constexpr uint32_t kKVTile = kBN * D * 2;
   static constexpr uint32_t kPTile = kPTmem ? 0 : kBM * kBN * 2;
-  static constexpr uint32_t kColP = 2 * kBN;
-  static constexpr uint32_t kColO = kPTmem ? 3 * kBN : 2 * kBN;
-  static_assert(kColO + 2 * D <= 512, "tensor memory budget");
+  static constexpr uint32_t kColP = KT * kBN;
+  static constexpr uint32_t kColO = kPTmem ? KT * (kBN + kBN / 2) : KT * kBN;
+  // two tiles take all 512 columns; one tile 256, so two CTAs can share an SM
+  static constexpr uint32_t kTmemCols = KT == 2 ? 512 : 256;
+  static_assert(kColO + KT * D <= kTmemCols, "tensor memory budget");
   static constexpr uint32_t kQ = 0;
-  static constexpr uint32_t kP = kQ + 2 * kQTile;
-  static constexpr uint32_t kKV = kP + 2 * kPTile;
-  static constexpr int kStages = kPTmem ? 10 : 3;
+  static constexpr uint32_t kP = kQ + KT * kQTile;
+  static constexpr uint32_t kKV = kP + KT * kPTile;
+  static constexpr int kStages = kPTmem ? (KT == 2 ? 10 : 5) : 3;
   static constexpr uint32_t kBar = kKV + kStages * kKVTile;
   static constexpr int kNumBars = 1 + 2 * kStages + 8 + 1;
   static constexpr uint32_t kMisc = kBar + kNumBars * 8;  // [tmem base][abort][schedule x 8]
   static constexpr uint32_t kBytes = kMisc + 64 + 1024;   // + slack to align the base to 1024
-  static_assert(kBytes <= 232448, "shared memory budget");
+  static_assert(kBytes <= (KT == 2 ? 232448 : 232448 / 2 - 1024), "shared memory budget");
 };
 
 // Position in the K/V load sequence K0, K1, V0, K2, V1, ..., V(n-1): keys run
@@ -176,9 +180,18 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatil
   return __all_sync(0xffffffffu, ok);
 }
 
-template <typename T, int D, bool CAUSAL, bool VARLEN>
-__global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_constant__ FmhaArgs a) {
-  using Lay = Layout<D>;
+template <typename T, int D, bool CAUSAL, bool VARLEN, int KT>
+__global__ void __launch_bounds__(threads_for<KT>(), 3 - KT) fmha_fwd_kernel(const __grid_constant__ FmhaArgs a) {
+  using Lay = Layout<D, KT>;
+  constexpr int kThreads = threads_for<KT>();
+  static_assert(KT == 2 || VARLEN, "one query tile per CTA is the varlen (ViT) form");
+  // register split between warpgroup 0 (producer, MMA) and the softmax
+  // warpgroups: the launch allocation is 65536 / (threads x CTAs per SM)
+  // registers a thread, kept in total
+  constexpr uint32_t kRegsLow = KT == 2 ? 104 : 56;
+  constexpr uint32_t kRegsHigh = KT == 2 ? 200 : 200;
+  static_assert(KT == 2 ? 128 * kRegsLow + 256 * kRegsHigh <= 384 * 168 : kRegsLow + kRegsHigh <= 2 * 128,
+                "register split");
   constexpr int NS = Lay::kStages;
   constexpr int kBN = Lay::kBN;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
@@ -231,8 +244,8 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
     q_len = kv_len = a.seq_q;
   } else {
     if (warp == 0) {
-      // find (sequence, row-pair block) of this CTA: prefix sums of
-      // ceil(len_q / 256) over the sequences, 32 sequences per step
+      // find (sequence, row block of KT x 128 rows) of this CTA: prefix sums
+      // of ceil(len_q / (KT x 128)) over the sequences, 32 sequences per step
       const int H = a.hq;
       int target = blockIdx.x / H;
       int found = -1, pr = 0, qs = 0, ql = 0, ks = 0, kl = 0;
@@ -244,7 +257,7 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
           qei = min(max(a.cu_q[i + 1], qsi), a.seq_q);
           ksi = min(max(a.cu_k[i], 0), a.seq_kv);
           kei = min(max(a.cu_k[i + 1], ksi), a.seq_kv);
-          np = (qei - qsi + 2 * kBM - 1) / (2 * kBM);
+          np = (qei - qsi + KT * kBM - 1) / (KT * kBM);
         }
         int incl = np;
 #pragma unroll
@@ -278,7 +291,7 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
     __syncthreads();
     if (sched[0] < 0) return;  // past the last tile (uniform)
     head0 = head1 = kvh = blockIdx.x % a.hq;
-    row0 = sched[1] * 2 * kBM;
+    row0 = sched[1] * KT * kBM;
     row1 = row0 + kBM;
     q_base = sched[2];
     q_len = sched[3];
@@ -297,7 +310,7 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
       mbar_init(kv_full(s), 1);
       mbar_init(kv_empty(s), 1);
     }
-    for (int t = 0; t < 2; ++t) {
+    for (int t = 0; t < KT; ++t) {
       mbar_init(s_full(t), 1);
       mbar_init(p_full(t), 128);
       mbar_init(o_full(t), 1);
@@ -307,30 +320,31 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
     fence_mbar_init();
   }
   if (warp == 1) {
-    tc::tmem_alloc(sb + Lay::kMisc, 512);
+    tc::tmem_alloc(sb + Lay::kMisc, Lay::kTmemCols);
     tc::tmem_relinquish();
   }
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
-  if (threadIdx.x == 0 && (tmem & 0xFFFFu) != 0u) {  // a 512-column allocation starts at column 0
+  // the allocation starts at lane 0 and at a multiple of its size (column 0,
+  // or 256 for the second of two 256-column allocations on an SM)
+  if (threadIdx.x == 0 && ((tmem >> 16) != 0u || (tmem & 0xFFFFu) % Lay::kTmemCols != 0u ||
+                           (tmem & 0xFFFFu) + Lay::kTmemCols > 512u)) {
     flag_device_error(a.err, AICAS_DEVERR_TMEM);
     *abort_flag = 1;
   }
   __syncthreads();
   if (warp < 4) {
-    // register split: 104 per thread here, 200 in the softmax warpgroups
-    // (128 x 104 + 256 x 200 = 64512 = 384 x 168, the launch allocation)
-    tc::regs_dec<104>();
+    tc::regs_dec<kRegsLow>();
     if (warp == 0) {
       // ------------------------------------------------------------ TMA producer
       if (lane == 0 && !*abort_flag) {
         tma_prefetch_desc(&a.tm_q);
         tma_prefetch_desc(&a.tm_k);
         tma_prefetch_desc(&a.tm_v);
-        mbar_arrive_expect_tx(q_full, 2 * Lay::kQTile);
-        for (int t = 0; t < 2; ++t)
+        mbar_arrive_expect_tx(q_full, KT * Lay::kQTile);
+        for (int t = 0; t < KT; ++t)
           for (int bx = 0; bx < D / 64; ++bx)
             tma_tile(sb + Lay::kQ + t * Lay::kQTile + bx * (kBM * 128), &a.tm_q, a.q_rows_first, bx * 64,
                      q_base + (t ? row1 : row0), t ? head1 : head0, b, q_full);
@@ -406,49 +420,79 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
         bool ok = !*abort_flag && mbar_wait(q_full, 0, abort_flag, a.err);
         if (ok && n_kv > 0) {
           ok = mbar_wait(kv_full(0), 0, abort_flag, a.err);
-          if (ok) {
-            tc::fence_after_sync();
-            issue_s(0, 0);
-            tc::commit(s_full(0));
-            issue_s(0, 1);
-            tc::commit(s_full(1));
-            tc::commit(kv_empty(0));
-          }
-          for (int j = 0; ok && j < n_kv; ++j) {
-            const int iv = kv_load_index_v(j, n_kv), ik = kv_load_index_k(j + 1);
-            const int sv = iv % NS, sk = ik % NS;
-            const bool more = j + 1 < n_kv;
-            // Per-tile order, as the softmax groups release their inputs:
-            // S(j+1,0) as soon as group 0 has READ S(j,0) (not after its softmax),
-            // PV(j,0) once P(j,0) is written, then the same for tile 1.
-            if (more) {
-              ok = mbar_wait(kv_full(sk), (ik / NS) & 1, abort_flag, a.err) &&
-                   mbar_wait(s_free(0), j & 1, abort_flag, a.err);
-              if (!ok) break;
+          if constexpr (KT == 2) {
+            if (ok) {
               tc::fence_after_sync();
-              issue_s(sk, 0);
+              issue_s(0, 0);
               tc::commit(s_full(0));
+              issue_s(0, 1);
+              tc::commit(s_full(1));
+              tc::commit(kv_empty(0));
             }
-            ok = mbar_wait(kv_full(sv), (iv / NS) & 1, abort_flag, a.err) &&
-                 mbar_wait(p_full(0), j & 1, abort_flag, a.err);
-            if (!ok) break;
-            tc::fence_after_sync();
-            issue_pv(j, sv, 0);
-            tc::commit(o_full(0));
-            if (more) {
-              ok = mbar_wait(s_free(1), j & 1, abort_flag, a.err);
+            for (int j = 0; ok && j < n_kv; ++j) {
+              const int iv = kv_load_index_v(j, n_kv), ik = kv_load_index_k(j + 1);
+              const int sv = iv % NS, sk = ik % NS;
+              const bool more = j + 1 < n_kv;
+              // Per-tile order, as the softmax groups release their inputs:
+              // S(j+1,0) as soon as group 0 has READ S(j,0) (not after its softmax),
+              // PV(j,0) once P(j,0) is written, then the same for tile 1.
+              if (more) {
+                ok = mbar_wait(kv_full(sk), (ik / NS) & 1, abort_flag, a.err) &&
+                     mbar_wait(s_free(0), j & 1, abort_flag, a.err);
+                if (!ok) break;
+                tc::fence_after_sync();
+                issue_s(sk, 0);
+                tc::commit(s_full(0));
+              }
+              ok = mbar_wait(kv_full(sv), (iv / NS) & 1, abort_flag, a.err) &&
+                   mbar_wait(p_full(0), j & 1, abort_flag, a.err);
               if (!ok) break;
               tc::fence_after_sync();
-              issue_s(sk, 1);
-              tc::commit(s_full(1));
-              tc::commit(kv_empty(sk));
+              issue_pv(j, sv, 0);
+              tc::commit(o_full(0));
+              if (more) {
+                ok = mbar_wait(s_free(1), j & 1, abort_flag, a.err);
+                if (!ok) break;
+                tc::fence_after_sync();
+                issue_s(sk, 1);
+                tc::commit(s_full(1));
+                tc::commit(kv_empty(sk));
+              }
+              ok = mbar_wait(p_full(1), j & 1, abort_flag, a.err);
+              if (!ok) break;
+              tc::fence_after_sync();
+              issue_pv(j, sv, 1);
+              tc::commit(o_full(1));
+              tc::commit(kv_empty(sv));
             }
-            ok = mbar_wait(p_full(1), j & 1, abort_flag, a.err);
-            if (!ok) break;
-            tc::fence_after_sync();
-            issue_pv(j, sv, 1);
-            tc::commit(o_full(1));
-            tc::commit(kv_empty(sv));
+          } else {
+            // one tile: S(j+1) as soon as the softmax has read S(j), PV(j) once P(j) is written
+            if (ok) {
+              tc::fence_after_sync();
+              issue_s(0, 0);
+              tc::commit(s_full(0));
+              tc::commit(kv_empty(0));
+            }
+            for (int j = 0; ok && j < n_kv; ++j) {
+              const int iv = kv_load_index_v(j, n_kv), ik = kv_load_index_k(j + 1);
+              const int sv = iv % NS, sk = ik % NS;
+              if (j + 1 < n_kv) {
+                ok = mbar_wait(kv_full(sk), (ik / NS) & 1, abort_flag, a.err) &&
+                     mbar_wait(s_free(0), j & 1, abort_flag, a.err);
+                if (!ok) break;
+                tc::fence_after_sync();
+                issue_s(sk, 0);
+                tc::commit(s_full(0));
+                tc::commit(kv_empty(sk));
+              }
+              ok = mbar_wait(kv_full(sv), (iv / NS) & 1, abort_flag, a.err) &&
+                   mbar_wait(p_full(0), j & 1, abort_flag, a.err);
+              if (!ok) break;
+              tc::fence_after_sync();
+              issue_pv(j, sv, 0);
+              tc::commit(o_full(0));
+              tc::commit(kv_empty(sv));
+            }
           }
         }
         // all products issued so far have completed before the CTA tears down
@@ -461,7 +505,7 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
     // warpgroup 1 owns query tile 0, warpgroup 2 tile 1; a warp may only touch
     // the TMEM lanes of its rank within its warpgroup (warp % 4), which is the
     // quarter of the tile's rows it owns
-    tc::regs_inc<200>();
+    tc::regs_inc<kRegsHigh>();
     const int t = (warp - 4) >> 2;
     const int qw = warp & 3;
     const int r = qw * 32 + lane;
@@ -656,7 +700,7 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_fwd_kernel(const __grid_cons
   if (warp == 1) {
     __syncwarp();
     tc::fence_after_sync();
-    tc::tmem_dealloc(tmem, 512);
+    tc::tmem_dealloc(tmem, Lay::kTmemCols);
   }
 }
 
@@ -718,26 +762,36 @@ bool make_map(CUtensorMap* m, const void* ptr, bool bf16, int d, int rows, int h
   return true;
 }
 
-template <typename T, int D, bool CAUSAL, bool VARLEN>
+template <typename T, int D, bool CAUSAL, bool VARLEN, int KT>
 cudaError_t launch_t(const FmhaArgs& a, int grid, cudaStream_t st) {
-  auto kern = fmha_fwd_kernel<T, D, CAUSAL, VARLEN>;
+  auto kern = fmha_fwd_kernel<T, D, CAUSAL, VARLEN, KT>;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Layout<D>::kBytes);
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Layout<D, KT>::kBytes);
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
-  kern<<<grid, kThreads, Layout<D>::kBytes, st>>>(a);
+  kern<<<grid, threads_for<KT>(), Layout<D, KT>::kBytes, st>>>(a);
   return cudaGetLastError();
 }
 
+// Query tiles per CTA of the varlen kernel at head_dim 64 (the ViT): one, so
+// that two CTAs share an SM and each hides the other's fill and drain.
+#ifndef AICAS_VARLEN64_TILES
+#define AICAS_VARLEN64_TILES 1
+#endif
+constexpr int kVarlen64Tiles = AICAS_VARLEN64_TILES;
+
+int tiles_per_cta(int d, bool varlen) { return (varlen && d == 64) ? kVarlen64Tiles : 2; }
+
 template <typename T>
 cudaError_t dispatch(int d, bool varlen, const FmhaArgs& a, int grid, cudaStream_t st) {
-  if (d == 128) return varlen ? launch_t<T, 128, false, true>(a, grid, st) : launch_t<T, 128, true, false>(a, grid, st);
-  return varlen ? launch_t<T, 64, false, true>(a, grid, st) : launch_t<T, 64, true, false>(a, grid, st);
+  if (d == 128)
+    return varlen ? launch_t<T, 128, false, true, 2>(a, grid, st) : launch_t<T, 128, true, false, 2>(a, grid, st);
+  return varlen ? launch_t<T, 64, false, true, kVarlen64Tiles>(a, grid, st) : launch_t<T, 64, true, false, 2>(a, grid, st);
 }
 
 }  // namespace
@@ -750,7 +804,7 @@ int run_fmha(const aicas_fmha_params* p, bool varlen, cudaStream_t stream, unsig
   const bool bf16 = p->dtype == AICAS_DTYPE_BF16;
   FmhaArgs a;
   memset(&a, 0, sizeof(a));
-  const int kv_box = Layout<128>::kBN;
+  const int kv_box = Layout<128, 2>::kBN;
   if (!make_map(&a.tm_q, p->q, bf16, p->head_dim, p->seq_len_q, p->num_q_heads, p->batch, p->q_stride_b,
                 p->q_stride_h, p->q_stride_s, kBM, &a.q_rows_first, err, errlen) ||
       !make_map(&a.tm_k, p->k, bf16, p->head_dim, p->seq_len_kv, p->num_kv_heads, p->batch, p->k_stride_b,
@@ -776,7 +830,8 @@ int run_fmha(const aicas_fmha_params* p, bool varlen, cudaStream_t stream, unsig
     a.cu_k = p->cu_seqlens_k;
     a.num_seqs = p->num_seqs;
     if (p->num_seqs == 0) return AICAS_OK;
-    grid = ((long long)(p->seq_len_q + 2 * kBM - 1) / (2 * kBM) + p->num_seqs) * p->num_q_heads;
+    const int rows = tiles_per_cta(p->head_dim, true) * kBM;
+    grid = ((long long)(p->seq_len_q + rows - 1) / rows + p->num_seqs) * p->num_q_heads;
   } else {
     a.pair_heads = (a.group % 2 == 0) ? 1 : 0;
     a.num_m = a.pair_heads ? (p->seq_len_q + kBM - 1) / kBM : (p->seq_len_q + 2 * kBM - 1) / (2 * kBM);
