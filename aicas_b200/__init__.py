@@ -3,11 +3,13 @@
 Public surface = the reference package ``triton_qwen3vl``'s ``__all__``
 (triton_qwen3vl/__init__.py:1-16 in the reference project) plus the operators
 it leaves to Hugging Face or lacks: :func:`rope_kv_append`,
-:func:`gqa_decode_partial` and :func:`merge_partials`.
+:func:`gqa_decode_partial` and :func:`merge_partials`, and the decode-side
+products of its native decode path (:func:`decode_linear`).
 """
 from . import _native
 from .backends import TEXT_BACKEND_KEY, VISION_BACKEND_KEY, text_triton_attention, vision_triton_attention
 from .ops import (
+    decode_linear,
     gqa_decode_attention,
     gqa_decode_partial,
     gqa_flash_attention,
@@ -27,6 +29,7 @@ __all__ = [
     "TEXT_BACKEND_KEY",
     "TRITON_AVAILABLE",
     "VISION_BACKEND_KEY",
+    "decode_linear",
     "gqa_decode_attention",
     "gqa_decode_partial",
     "gqa_flash_attention",

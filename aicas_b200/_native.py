@@ -33,6 +33,14 @@ CAP_PREFILL_TCGEN05 = 4
 CAP_VARLEN_TCGEN05 = 8
 CAP_ROPE_APPEND = 16
 CAP_PEER_EXCHANGE = 32
+CAP_DECODE_LINEAR = 64
+
+LINEAR_MAX_SEGMENTS = 4
+LINEAR_MAX_ROWS = 32
+LINEAR_STORE = 0
+LINEAR_RESIDUAL = 1
+LINEAR_SWIGLU = 2
+LINEAR_NO_PDL = 1
 
 _i64 = ctypes.c_int64
 _i32 = ctypes.c_int32
@@ -105,6 +113,20 @@ class RopeAppendParams(ctypes.Structure):
     ]
 
 
+class LinearSegment(ctypes.Structure):
+    _fields_ = [("weight", _vp), ("weight_stride", _i64), ("out", _vp), ("out_stride", _i64), ("rows", _i32)]
+
+
+class LinearParams(ctypes.Structure):
+    _fields_ = [
+        ("x", _vp), ("x_stride", _i64), ("batch", _i32), ("in_features", _i32),
+        ("norm_weight", _vp), ("eps", _f32), ("mode", _i32),
+        ("residual", _vp), ("residual_stride", _i64),
+        ("num_segments", _i32), ("seg", LinearSegment * LINEAR_MAX_SEGMENTS),
+        ("dtype", _i32), ("flags", _i32),
+    ]
+
+
 # name -> (restype, argtypes); exactly the functions declared in include/aicas_b200.h
 EXPORTS = {
     "aicas_decode_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(DecodeParams)]),
@@ -120,6 +142,8 @@ EXPORTS = {
     "aicas_prefill_gqa_causal": (ctypes.c_int, [ctypes.POINTER(FmhaParams), _vp]),
     "aicas_varlen_attention": (ctypes.c_int, [ctypes.POINTER(FmhaParams), _vp]),
     "aicas_rope_kv_append": (ctypes.c_int, [ctypes.POINTER(RopeAppendParams), _vp]),
+    "aicas_linear_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(LinearParams)]),
+    "aicas_decode_linear": (ctypes.c_int, [ctypes.POINTER(LinearParams), _vp, ctypes.c_size_t, _vp]),
     "aicas_version": (ctypes.c_char_p, []),
     "aicas_capabilities": (ctypes.c_uint32, []),
     "aicas_last_error": (ctypes.c_char_p, []),

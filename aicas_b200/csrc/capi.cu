@@ -9,6 +9,7 @@
 
 #include "common.cuh"
 #include "fmha.cuh"
+#include "linear.cuh"
 
 namespace aicas {
 
@@ -250,13 +251,57 @@ int noalloc_scratch(void** out) {
 
 }  // namespace
 
+int check_linear(const aicas_linear_params* p) {
+  if (p == nullptr) return fail(AICAS_ERR_INVALID, "params is NULL");
+  if (p->dtype != AICAS_DTYPE_F16 && p->dtype != AICAS_DTYPE_BF16)
+    return fail(AICAS_ERR_UNSUPPORTED, "decode linear needs fp16 or bf16 (dtype %d)", p->dtype);
+  if (p->batch < 0 || p->batch > AICAS_LINEAR_MAX_ROWS)
+    return fail(AICAS_ERR_UNSUPPORTED, "decode linear takes 0..%d rows (got %d)", AICAS_LINEAR_MAX_ROWS, p->batch);
+  if (p->in_features <= 0 || p->in_features % 8 != 0)
+    return fail(AICAS_ERR_UNSUPPORTED, "in_features must be a positive multiple of 8 (got %d)", p->in_features);
+  if (p->mode != AICAS_LINEAR_STORE && p->mode != AICAS_LINEAR_RESIDUAL && p->mode != AICAS_LINEAR_SWIGLU)
+    return fail(AICAS_ERR_INVALID, "unknown mode %d", p->mode);
+  if (p->num_segments < 1 || p->num_segments > AICAS_LINEAR_MAX_SEGMENTS)
+    return fail(AICAS_ERR_INVALID, "num_segments must be 1..%d (got %d)", AICAS_LINEAR_MAX_SEGMENTS, p->num_segments);
+  if (p->mode == AICAS_LINEAR_RESIDUAL && p->num_segments != 1)
+    return fail(AICAS_ERR_INVALID, "the residual epilogue takes one segment");
+  if (p->mode == AICAS_LINEAR_SWIGLU && (p->num_segments != 2 || p->seg[0].rows != p->seg[1].rows))
+    return fail(AICAS_ERR_INVALID, "the SwiGLU epilogue takes two segments (gate, up) with equal rows");
+  if (p->x == nullptr || !aligned16(p->x)) return fail(AICAS_ERR_INVALID, "x must be a 16-byte aligned pointer");
+  if (p->x_stride < p->in_features || !stride_ok(p->x_stride, 2))
+    return fail(AICAS_ERR_INVALID, "x_stride must be >= in_features and a multiple of 8 elements");
+  if (p->norm_weight != nullptr && !aligned16(p->norm_weight))
+    return fail(AICAS_ERR_INVALID, "norm_weight must be 16-byte aligned");
+  if (p->norm_weight != nullptr && !(p->eps >= 0.0f)) return fail(AICAS_ERR_INVALID, "eps must be >= 0");
+  for (int j = 0; j < p->num_segments; ++j) {
+    const aicas_linear_segment& g = p->seg[j];
+    if (g.weight == nullptr || !aligned16(g.weight))
+      return fail(AICAS_ERR_INVALID, "segment %d: weight must be a 16-byte aligned pointer", j);
+    if (g.weight_stride < p->in_features || !stride_ok(g.weight_stride, 2))
+      return fail(AICAS_ERR_INVALID, "segment %d: weight_stride must be >= in_features and a multiple of 8", j);
+    if (g.rows <= 0) return fail(AICAS_ERR_INVALID, "segment %d: rows must be positive", j);
+    const bool writes = p->mode != AICAS_LINEAR_SWIGLU || j == 0;
+    if (writes && (g.out == nullptr || (reinterpret_cast<uintptr_t>(g.out) & 1u) != 0))
+      return fail(AICAS_ERR_INVALID, "segment %d: out must be a 2-byte aligned pointer", j);
+    if (writes && p->batch > 1 && g.out_stride < g.rows)
+      return fail(AICAS_ERR_INVALID, "segment %d: out_stride must be >= rows", j);
+  }
+  if (p->mode == AICAS_LINEAR_RESIDUAL) {
+    if (p->residual == nullptr || (reinterpret_cast<uintptr_t>(p->residual) & 1u) != 0)
+      return fail(AICAS_ERR_INVALID, "the residual epilogue needs a 2-byte aligned residual");
+    if (p->batch > 1 && p->residual_stride < p->seg[0].rows)
+      return fail(AICAS_ERR_INVALID, "residual_stride must be >= rows");
+  }
+  return AICAS_OK;
+}
+
 extern "C" {
 
 const char* aicas_version(void) { return "aicas_b200 0.1.0 sm_100a abi 1"; }
 
 uint32_t aicas_capabilities(void) {
   return AICAS_CAP_DECODE | AICAS_CAP_MERGE | AICAS_CAP_ROPE_APPEND | AICAS_CAP_PEER_EXCHANGE |
-         aicas::fmha_capabilities();
+         AICAS_CAP_DECODE_LINEAR | aicas::fmha_capabilities();
 }
 
 const char* aicas_last_error(void) { return g_err; }
@@ -481,6 +526,20 @@ int aicas_varlen_attention(const aicas_fmha_params* p, void* stream) {
   int rc = check_fmha(p, true);
   if (rc != AICAS_OK) return rc;
   return aicas::run_fmha(p, /*varlen=*/true, static_cast<cudaStream_t>(stream), device_error_word(), g_err, sizeof(g_err));
+}
+
+size_t aicas_linear_workspace_bytes(const aicas_linear_params* p) {
+  if (check_linear(p) != AICAS_OK) return 0;
+  size_t bytes = 0;
+  if (aicas::plan_linear_workspace(p, sm_count(), &bytes, g_err, sizeof(g_err)) != AICAS_OK) return 0;
+  return bytes;
+}
+
+int aicas_decode_linear(const aicas_linear_params* p, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_linear(p);
+  if (rc != AICAS_OK) return rc;
+  return aicas::run_linear(p, sm_count(), workspace, workspace_bytes, static_cast<cudaStream_t>(stream),
+                           device_error_word(), g_err, sizeof(g_err));
 }
 
 }  // extern "C"

@@ -32,8 +32,23 @@
 #include "common.cuh"
 #include "fmha.cuh"
 #include "tcgen05.cuh"
+#include "tma_host.cuh"
 
 namespace aicas {
+
+EncodeTiledFn tensor_map_encoder() {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
 namespace {
 
 constexpr int kBM = 128;  // query rows per tile (MMA M)
@@ -706,28 +721,11 @@ __global__ void __launch_bounds__(threads_for<KT>(), 3 - KT) fmha_fwd_kernel(con
 
 // ------------------------------------------------------------------ host side
 
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  if (fn == nullptr) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  }
-  return fn;
-}
-
 // 4-D map over [B, heads, rows, D] (element strides), the two middle dimensions
 // ordered by increasing stride as the tensor-map encoder expects.
 bool make_map(CUtensorMap* m, const void* ptr, bool bf16, int d, int rows, int heads, int batch, int64_t s_b,
               int64_t s_h, int64_t s_s, int box_rows, int* rows_first, char* err, size_t errlen) {
-  EncodeTiledFn enc = encode_fn();
+  EncodeTiledFn enc = tensor_map_encoder();
   if (enc == nullptr) {
     snprintf(err, errlen, "cuTensorMapEncodeTiled is unavailable from the driver");
     return false;

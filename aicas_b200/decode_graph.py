@@ -13,6 +13,11 @@ version does differently:
   (:func:`aicas_b200.ops.rope_kv_append`) and the split-KV decode kernel,
   which reads the cache lengths from a device vector, so the graph holds no
   per-step host value;
+* every product of the step (q/k/v, o_proj, gate/up, down_proj, LM head) runs
+  on :func:`aicas_b200.ops.decode_linear` with the RMSNorms, the residual adds
+  and SiLU * up fused into it, as the reference's native decode ops fuse them
+  (dujunbaoV1/native_cuda_ops/decode_q1_gqa_kernel.cu:127-331), for batches
+  of up to 32 rows;
 * the step advances its own state on the device -- cache lengths, MRoPE
   position ids, the next token (argmax of the logits) and the token log -- so
   N new tokens are one prefill and N - 1 graph replays with no host work or
@@ -27,6 +32,7 @@ from __future__ import annotations
 import torch
 from transformers.cache_utils import Cache, CacheLayerMixin
 
+from . import _native as nat
 from . import ops
 
 
@@ -94,8 +100,9 @@ class GraphGreedyDecoder:
     ``model`` is a ``Qwen3VLForConditionalGeneration`` in eval mode on one GPU
     with 16-bit weights."""
 
-    def __init__(self, model):
+    def __init__(self, model, fused: bool = True):
         self.model = model
+        self.fused = fused
         self.lm = model.model.language_model
         self.lm_head = model.lm_head
         attn = self.lm.layers[0].self_attn
@@ -104,9 +111,45 @@ class GraphGreedyDecoder:
         self.head_dim = attn.head_dim
         self.group = attn.num_key_value_groups
         self.last_graph_replays = 0
+        self.last_step_ms = float("nan")
 
     def _step(self, st: dict) -> None:
         """One decode token for the whole batch, all state on the device."""
+        if self.fused and st["tok"].shape[0] <= nat.LINEAR_MAX_ROWS:
+            self._step_fused(st)
+        else:
+            self._step_modules(st)
+
+    def _step_fused(self, st: dict) -> None:
+        """The step with every product on :func:`aicas_b200.ops.decode_linear`:
+        per layer, RMSNorm + q/k/v, the fused q/k norm + RoPE + append, decode
+        attention, o_proj + residual, RMSNorm + gate/up + SiLU*up, down_proj +
+        residual; then the final RMSNorm + LM head."""
+        B, D = st["tok"].shape[0], self.head_dim
+        x = self.lm.embed_tokens(st["tok"]).view(B, -1)
+        cos, sin = self.lm.rotary_emb(x.view(B, 1, -1), st["pos"])
+        for i, layer in enumerate(self.lm.layers):
+            attn, mlp = layer.self_attn, layer.mlp
+            ln1, ln2 = layer.input_layernorm, layer.post_attention_layernorm
+            q, k, v = ops.decode_linear(x, (attn.q_proj.weight, attn.k_proj.weight, attn.v_proj.weight),
+                                        norm_weight=ln1.weight, eps=ln1.variance_epsilon)
+            kc, vc = st["caches"][i]
+            qr = ops.rope_kv_append(q.view(B, 1, self.hq, D).transpose(1, 2), k.view(B, 1, self.hkv, D).transpose(1, 2),
+                                    v.view(B, 1, self.hkv, D).transpose(1, 2), cos, sin, kc, vc, st["lens"],
+                                    kv_lens_out=st["lens_next"], q_norm_weight=attn.q_norm.weight,
+                                    k_norm_weight=attn.k_norm.weight, eps=attn.q_norm.variance_epsilon)
+            o = ops.gqa_decode_attention(qr, kc, vc, sm_scale=attn.scaling, num_key_value_groups=self.group,
+                                         kv_lens=st["lens_next"])
+            ops.decode_linear(o.reshape(B, self.hq * D), attn.o_proj.weight, residual=x, out=x)
+            h = ops.decode_linear(x, (mlp.gate_proj.weight, mlp.up_proj.weight), norm_weight=ln2.weight,
+                                  eps=ln2.variance_epsilon, swiglu=True)
+            ops.decode_linear(h, mlp.down_proj.weight, residual=x, out=x)
+        logits = ops.decode_linear(x, self.lm_head.weight, norm_weight=self.lm.norm.weight,
+                                   eps=self.lm.norm.variance_epsilon)
+        self._advance(st, logits)
+
+    def _step_modules(self, st: dict) -> None:
+        """The step through the model's own modules (any batch size)."""
         B, D = st["tok"].shape[0], self.head_dim
         x = self.lm.embed_tokens(st["tok"])
         cos, sin = self.lm.rotary_emb(x, st["pos"])
@@ -125,6 +168,11 @@ class GraphGreedyDecoder:
             x = x + attn.o_proj(o.transpose(1, 2).reshape(B, 1, self.hq * D))
             x = x + layer.mlp(layer.post_attention_layernorm(x))
         logits = self.lm_head(self.lm.norm(x)[:, -1])
+        self._advance(st, logits)
+
+    @staticmethod
+    def _advance(st: dict, logits: torch.Tensor) -> None:
+        B = st["tok"].shape[0]
         nxt = logits.argmax(-1).view(B, 1)
         st["tok"].copy_(nxt)
         st["step"].add_(1)
@@ -136,7 +184,32 @@ class GraphGreedyDecoder:
     def generate(self, inputs: dict, max_new_tokens: int) -> torch.Tensor:
         """``[B, max_new_tokens]`` greedy tokens after the prompts in ``inputs``
         (the processor's dict: input_ids, attention_mask of ones,
-        mm_token_type_ids, pixel_values, image_grid_thw)."""
+        mm_token_type_ids, pixel_values, image_grid_thw).  Afterwards
+        ``last_step_ms`` holds the mean device time of one replayed decode step
+        (CUDA events around the replays)."""
+        graph, st = self.prefill_and_capture(inputs, max_new_tokens)
+        if graph is None:
+            return st["log"]
+        device = st["log"].device
+        stream = torch.cuda.current_stream(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(max_new_tokens - 1):
+            graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize(device)
+        self.last_graph_replays = max_new_tokens - 1
+        self.last_step_ms = e0.elapsed_time(e1) / (max_new_tokens - 1)
+        result = st["log"].clone()
+        del graph
+        return result
+
+    @torch.no_grad()
+    def prefill_and_capture(self, inputs: dict, max_new_tokens: int):
+        """Runs the prefill and captures the decode step: ``(graph, state)``,
+        the graph ``None`` when one token was asked for.  Each replay of the
+        graph appends one token to ``state["log"]``; at most
+        ``max_new_tokens - 1`` replays fit the cache."""
         if max_new_tokens < 1:
             raise ValueError("max_new_tokens must be at least 1")
         ids = inputs["input_ids"]
@@ -152,7 +225,7 @@ class GraphGreedyDecoder:
         log = torch.zeros(B, max_new_tokens, dtype=torch.long, device=device)
         log[:, 0] = first
         if max_new_tokens == 1:
-            return log
+            return None, {"log": log}
         deltas = self.model.model.rope_deltas.to(device=device, dtype=torch.long).view(B)
         st = {
             "tok": first.view(B, 1).clone(),
@@ -184,10 +257,4 @@ class GraphGreedyDecoder:
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=stream):
             self._step(st)
-        for _ in range(max_new_tokens - 1):
-            graph.replay()
-        self.last_graph_replays = max_new_tokens - 1
-        torch.cuda.synchronize(device)
-        result = st["log"].clone()
-        del graph
-        return result
+        return graph, st

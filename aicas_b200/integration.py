@@ -175,6 +175,7 @@ class GenerateRun:
     tokens: torch.Tensor  # [B, new] generated ids
     seconds: float  # whole generate() call, device-synchronised
     ttft_seconds: float  # generate() of one new token (prefill + first sample)
+    step_ms: float = float("nan")  # device time of one decode step, where the path measures it
 
     @property
     def tokens_per_s(self) -> float:
@@ -236,7 +237,7 @@ def graph_generate(model, inputs: dict, max_new_tokens: int, timed: bool = True)
     t0 = time.perf_counter()
     tokens = dec.generate(inputs, max_new_tokens)
     _sync(device)
-    return GenerateRun(tokens=tokens, seconds=time.perf_counter() - t0, ttft_seconds=ttft)
+    return GenerateRun(tokens=tokens, seconds=time.perf_counter() - t0, ttft_seconds=ttft, step_ms=dec.last_step_ms)
 
 
 @torch.no_grad()
@@ -293,6 +294,7 @@ def run_check(batch: int = 8, seq_len: int = 2048, max_new_tokens: int = 128, gr
         "patched": {"tokens_per_s": ours.tokens_per_s, "seconds": ours.seconds, "ttft_s": ours.ttft_seconds},
         "sdpa": {"tokens_per_s": ref.tokens_per_s, "seconds": ref.seconds, "ttft_s": ref.ttft_seconds},
         "graph_decode": {"tokens_per_s": graph.tokens_per_s, "seconds": graph.seconds, "ttft_s": graph.ttft_seconds,
+                         "step_ms": graph.step_ms,
                          "token_match_vs_patched": token_match(graph.tokens, ours.tokens),
                          "max_logit_gap": float(gap_graph.max()), "mean_logit_gap": float(gap_graph.mean())},
     }

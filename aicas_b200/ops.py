@@ -473,3 +473,137 @@ def varlen_flash_attention(
 
     _call_in_device(query.device, run)
     return out
+
+
+# ---------------------------------------------------------------------- decode-side products
+
+# workspace of the decode-side products, one zero-initialised buffer per
+# (device, stream); the kernel leaves its tile counters zeroed after every call
+_LINEAR_WORKSPACES: dict[tuple[int, int], torch.Tensor] = {}
+
+_LINEAR_DTYPES = {torch.float16: nat.DTYPE_F16, torch.bfloat16: nat.DTYPE_BF16}
+
+
+def _linear_workspace(device: torch.device, stream: int, nbytes: int) -> torch.Tensor:
+    key = (device.index, stream)
+    ws = _LINEAR_WORKSPACES.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.zeros(max(nbytes, 4 << 20), dtype=torch.uint8, device=device)
+        _LINEAR_WORKSPACES[key] = ws
+    return ws
+
+
+def _overlaps(a: torch.Tensor, b: torch.Tensor) -> bool:
+    if a.untyped_storage().data_ptr() != b.untyped_storage().data_ptr():
+        return False
+    a0, b0 = a.data_ptr(), b.data_ptr()
+    a1 = a0 + ((a.shape[0] - 1) * a.stride(0) + a.shape[-1]) * a.element_size() if a.numel() else a0
+    b1 = b0 + ((b.shape[0] - 1) * b.stride(0) + b.shape[-1]) * b.element_size() if b.numel() else b0
+    return a0 < b1 and b0 < a1
+
+
+def _row_major(t: torch.Tensor, what: str) -> torch.Tensor:
+    if t.ndim != 2:
+        raise ValueError(f"{what} must be 2-D")
+    if t.stride(1) == 1 and _aligned(t, (t.stride(0),)):
+        return t
+    return t.contiguous()
+
+
+def decode_linear(
+    x: torch.Tensor,
+    weights: torch.Tensor | Sequence[torch.Tensor],
+    *,
+    norm_weight: torch.Tensor | None = None,
+    eps: float = 1e-6,
+    residual: torch.Tensor | None = None,
+    swiglu: bool = False,
+    out: torch.Tensor | Sequence[torch.Tensor] | None = None,
+    pdl: bool = True,
+):
+    """Weight-streaming products for the few rows of a decode step, on the
+    tensor cores, with the neighbouring elementwise work fused:
+
+    * ``x`` ``[R, K]`` (R <= 32), ``weights`` one ``[N, K]`` tensor or a list of
+      them (one read of x for all, as qkv_linear_matvec_kernel and
+      dual_linear_matvec_kernel in dujunbaoV1/native_cuda_ops/
+      decode_q1_gqa_kernel.cu:222-331 do); returns ``x' W^T`` per weight.
+    * ``norm_weight``: x' = Qwen3VLTextRMSNorm(x) with that weight and ``eps``
+      (rmsnorm_kernel :127-157, rounded as HF rounds), else x' = x.
+    * ``residual`` ``[R, N]``: returns ``residual + x' W^T`` (one weight), the
+      residual add of Qwen3VLTextDecoderLayer; ``out=residual`` updates it in
+      place.
+    * ``swiglu=True`` with ``weights=(gate, up)``: returns
+      ``silu(x' Wg^T) * (x' Wu^T)`` (gate_up_silu_matvec_kernel :174-220,
+      rounded as HF Qwen3VLTextMLP rounds).
+
+    Every tensor is fp16 or bf16 of one dtype with unit stride on the last
+    dimension.  Inputs the kernel cannot take raise ``ValueError``.
+    """
+    single = isinstance(weights, torch.Tensor)
+    ws_list = [weights] if single else list(weights)
+    if not ws_list:
+        raise ValueError("decode_linear needs at least one weight")
+    tensors = [x, *ws_list] + [t for t in (norm_weight, residual) if t is not None]
+    _reject_grad(*tensors)
+    if not all(t.is_cuda for t in tensors):
+        raise ValueError("decode_linear needs CUDA tensors")
+    if x.dtype not in _LINEAR_DTYPES or any(t.dtype != x.dtype for t in tensors):
+        raise ValueError("decode_linear needs fp16 or bf16 tensors of one dtype")
+    x = _row_major(x, "x")
+    R, K = x.shape
+    if R > nat.LINEAR_MAX_ROWS:
+        raise ValueError(f"decode_linear takes at most {nat.LINEAR_MAX_ROWS} rows (got {R})")
+    if len(ws_list) > nat.LINEAR_MAX_SEGMENTS:
+        raise ValueError(f"decode_linear takes at most {nat.LINEAR_MAX_SEGMENTS} weights")
+    ws_list = [_row_major(w, "weight") for w in ws_list]
+    if any(w.shape[1] != K for w in ws_list):
+        raise ValueError("every weight must be [N, in_features] with in_features == x.shape[1]")
+    if swiglu and (len(ws_list) != 2 or ws_list[0].shape != ws_list[1].shape):
+        raise ValueError("swiglu needs weights=(gate, up) of one shape")
+    if residual is not None and (swiglu or len(ws_list) != 1):
+        raise ValueError("residual takes exactly one weight")
+    if norm_weight is not None and (norm_weight.shape != (K,) or not norm_weight.is_contiguous()):
+        raise ValueError(f"norm_weight must be a contiguous [{K}] tensor")
+    n_out = 1 if swiglu else len(ws_list)
+    rows = [w.shape[0] for w in ws_list]
+    if out is None:
+        outs = [torch.empty((R, rows[i]), dtype=x.dtype, device=x.device) for i in range(n_out)]
+    else:
+        outs = [out] if isinstance(out, torch.Tensor) else list(out)
+        if len(outs) != n_out or any(o.shape != (R, rows[i]) or o.stride(1) != 1 or o.dtype != x.dtype
+                                     for i, o in enumerate(outs)):
+            raise ValueError("out does not match the outputs")
+    if residual is not None and (residual.shape != (R, rows[0]) or residual.stride(1) != 1):
+        raise ValueError(f"residual must be [{R}, {rows[0]}] with unit stride on the last dimension")
+    # every CTA reads all of x while others already write their outputs
+    for o in outs:
+        if _overlaps(o, x) or (norm_weight is not None and _overlaps(o, norm_weight)):
+            raise ValueError("decode_linear outputs must not overlap x or norm_weight")
+    p = nat.LinearParams()
+    p.x, p.x_stride, p.batch, p.in_features = x.data_ptr(), x.stride(0), R, K
+    p.norm_weight, p.eps = _ptr(norm_weight), float(eps)
+    p.mode = nat.LINEAR_SWIGLU if swiglu else (nat.LINEAR_RESIDUAL if residual is not None else nat.LINEAR_STORE)
+    if residual is not None:
+        p.residual, p.residual_stride = residual.data_ptr(), residual.stride(0)
+    p.num_segments = len(ws_list)
+    for i, w in enumerate(ws_list):
+        p.seg[i].weight, p.seg[i].weight_stride, p.seg[i].rows = w.data_ptr(), w.stride(0), w.shape[0]
+        o = outs[min(i, n_out - 1)]
+        p.seg[i].out, p.seg[i].out_stride = o.data_ptr(), o.stride(0)
+    p.dtype = _LINEAR_DTYPES[x.dtype]
+    p.flags = 0 if pdl else nat.LINEAR_NO_PDL
+    device = x.device
+
+    def run():
+        lib = nat.lib()
+        stream = _stream_handle(device)
+        nbytes = int(lib.aicas_linear_workspace_bytes(ctypes.byref(p)))
+        if nbytes == 0 and R > 0:
+            nat.check(nat.ERR_UNSUPPORTED, "aicas_linear_workspace_bytes")
+        ws = _linear_workspace(device, stream, nbytes)
+        nat.check(lib.aicas_decode_linear(ctypes.byref(p), ws.data_ptr(), ws.numel(), stream), "aicas_decode_linear")
+
+    if R > 0:
+        _call_in_device(device, run)
+    return outs[0] if (single or swiglu) else tuple(outs)

@@ -35,6 +35,16 @@
  *                             (InplaceDecodeCacheLayer.update); optional per-head
  *                             RMSNorm as in dujunbaoV1/native_cuda_ops/
  *                             decode_q1_gqa_kernel.cu:376-480
+ *   aicas_decode_linear       the decode-side matrix-vector products of
+ *                             dujunbaoV1/native_cuda_ops/decode_q1_gqa_kernel.cu:
+ *                             rmsnorm_kernel :127-157 (as a fused prologue),
+ *                             gate_up_silu_matvec_kernel :174-220 (SWIGLU),
+ *                             dual_linear_matvec_kernel :222-269 and
+ *                             qkv_linear_matvec_kernel :271-331 (segments),
+ *                             lm_head_argmax_stage1/2 :482-575 (the LM-head
+ *                             product; argmax stays with the caller), plus the
+ *                             residual add of HF Qwen3VLTextDecoderLayer
+ *                             (modeling_qwen3_vl.py:545-563)
  *
  * Layout conventions: attention tensors are 4-D [batch, heads, tokens, head_dim]
  * with head_dim contiguous (stride 1).  Strides are given in ELEMENTS.  All
@@ -244,6 +254,49 @@ typedef struct aicas_rope_append_params {
 AICAS_API int aicas_rope_kv_append(const aicas_rope_append_params* p, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* Decode-side weight-streaming products: Y = epilogue(X' W^T) for a few rows */
+/* X (the batch of one decode step) on the tensor cores.                      */
+/* ------------------------------------------------------------------------ */
+#define AICAS_LINEAR_MAX_SEGMENTS 4
+#define AICAS_LINEAR_MAX_ROWS 32
+#define AICAS_LINEAR_STORE 0    /* out_i = X' W_i^T for every segment i */
+#define AICAS_LINEAR_RESIDUAL 1 /* out = residual + round(X' W^T) (one segment; out may alias residual) */
+#define AICAS_LINEAR_SWIGLU 2   /* out = silu(round(X' Wg^T)) * round(X' Wu^T): segment 0 gate, 1 up */
+#define AICAS_LINEAR_NO_PDL 1   /* flags: launch without programmatic dependent launch */
+
+typedef struct aicas_linear_segment {
+  const void* weight;    /* [rows, in_features] with weight_stride elements between rows */
+  int64_t weight_stride;
+  void* out;             /* [batch, rows] with out_stride elements between batch rows */
+  int64_t out_stride;
+  int32_t rows;          /* output features of this segment */
+} aicas_linear_segment;
+
+typedef struct aicas_linear_params {
+  const void* x;         /* [batch, in_features], x_stride elements between rows */
+  int64_t x_stride;
+  int32_t batch;         /* 1 .. AICAS_LINEAR_MAX_ROWS (0: nothing to do) */
+  int32_t in_features;   /* multiple of 8 */
+  const void* norm_weight; /* optional [in_features]: X' = RMSNorm(X) * norm_weight, rounded as
+                              HF Qwen3VLTextRMSNorm rounds (modeling_qwen3_vl.py:398-403);
+                              NULL: X' = X */
+  float eps;
+  int32_t mode;          /* AICAS_LINEAR_* */
+  const void* residual;  /* RESIDUAL: [batch, rows] */
+  int64_t residual_stride;
+  int32_t num_segments;  /* 1 .. 4 (SWIGLU: 2, equal rows) */
+  aicas_linear_segment seg[AICAS_LINEAR_MAX_SEGMENTS];
+  int32_t dtype;         /* AICAS_DTYPE_F16 or AICAS_DTYPE_BF16, shared by every tensor */
+  int32_t flags;         /* AICAS_LINEAR_NO_PDL */
+} aicas_linear_params;
+
+/* Bytes of zero-initialised workspace aicas_decode_linear needs (tile counters
+   and split partials); the kernel leaves the counters zeroed again. */
+AICAS_API size_t aicas_linear_workspace_bytes(const aicas_linear_params* p);
+AICAS_API int aicas_decode_linear(const aicas_linear_params* p, void* workspace, size_t workspace_bytes,
+                                  void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* Library queries.                                                           */
 /* ------------------------------------------------------------------------ */
 /* "aicas_b200 <version> sm_100a abi <n>" */
@@ -256,6 +309,7 @@ AICAS_API const char* aicas_version(void);
 #define AICAS_CAP_VARLEN_TCGEN05 8u
 #define AICAS_CAP_ROPE_APPEND 16u
 #define AICAS_CAP_PEER_EXCHANGE 32u
+#define AICAS_CAP_DECODE_LINEAR 64u
 AICAS_API uint32_t aicas_capabilities(void);
 
 /* Message of the last failed call on this thread ("" if none). */

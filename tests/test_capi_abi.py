@@ -40,7 +40,7 @@ def test_version_and_capabilities(native_lib):
     assert v.startswith("aicas_b200 ") and "sm_100a" in v
     caps = nat.capabilities()
     assert caps & nat.CAP_DECODE and caps & nat.CAP_MERGE and caps & nat.CAP_ROPE_APPEND
-    assert caps & nat.CAP_PEER_EXCHANGE
+    assert caps & nat.CAP_PEER_EXCHANGE and caps & nat.CAP_DECODE_LINEAR
 
 
 STRUCTS = {
@@ -49,6 +49,8 @@ STRUCTS = {
     "aicas_fmha_params": nat.FmhaParams,
     "aicas_rope_append_params": nat.RopeAppendParams,
     "aicas_exchange_params": nat.ExchangeParams,
+    "aicas_linear_segment": nat.LinearSegment,
+    "aicas_linear_params": nat.LinearParams,
 }
 
 
@@ -192,3 +194,65 @@ def test_exchange_buffer_size_and_validation(native_lib):
     assert "multiple of 4" in nat.last_error()
     assert native_lib.aicas_peer_buffer_alloc(0, None, None) == nat.ERR_INVALID
     assert native_lib.aicas_peer_buffer_open(None, None) == nat.ERR_INVALID
+
+
+def _linear_params(R=8, K=2048, rows=(2048, 1024, 1024), mode=nat.LINEAR_STORE) -> nat.LinearParams:
+    p = nat.LinearParams()
+    base = 1 << 20  # fake, aligned; never dereferenced (validation and sizing only)
+    p.x, p.x_stride, p.batch, p.in_features = base, K, R, K
+    p.mode, p.dtype, p.eps = mode, nat.DTYPE_BF16, 1e-6
+    p.num_segments = len(rows)
+    for i, n in enumerate(rows):
+        p.seg[i].weight, p.seg[i].weight_stride, p.seg[i].rows = base * (2 + i), K, n
+        p.seg[i].out, p.seg[i].out_stride = base * (8 + i), n
+    return p
+
+
+def test_linear_workspace_size(native_lib):
+    # stream-K over (tile, 64-K block) units, one CTA per SM (148 without a GPU):
+    # a fixed 64 KiB region of tile counters + two fp32 partial slots per CTA
+    p = _linear_params()
+    grid = min(148, 32 * 32)
+    assert native_lib.aicas_linear_workspace_bytes(ctypes.byref(p)) == 65536 + 2 * grid * 16 * 128 * 4
+    p = _linear_params(R=20, K=6144, rows=(2048,), mode=nat.LINEAR_RESIDUAL)
+    p.residual, p.residual_stride = 9 << 20, 2048
+    assert native_lib.aicas_linear_workspace_bytes(ctypes.byref(p)) == 65536 + 2 * 148 * 32 * 128 * 4
+    p = _linear_params(rows=(6144, 6144), mode=nat.LINEAR_SWIGLU)
+    assert native_lib.aicas_linear_workspace_bytes(ctypes.byref(p)) == 65536 + 2 * 148 * 2 * 16 * 128 * 4
+    p = _linear_params(rows=(151936,))
+    assert native_lib.aicas_linear_workspace_bytes(ctypes.byref(p)) == 65536 + 2 * 148 * 16 * 128 * 4
+    p = _linear_params(rows=(16384 * 128 + 1,))  # more tiles than the counter region holds
+    assert native_lib.aicas_linear_workspace_bytes(ctypes.byref(p)) == 0
+    assert "exceed" in nat.last_error()
+
+
+@pytest.mark.parametrize(
+    "over, code, text",
+    [
+        ({"batch": 33}, nat.ERR_UNSUPPORTED, "0..32 rows"),
+        ({"in_features": 100, "x_stride": 100}, nat.ERR_UNSUPPORTED, "multiple of 8"),
+        ({"dtype": nat.DTYPE_F32}, nat.ERR_UNSUPPORTED, "fp16 or bf16"),
+        ({"mode": 9}, nat.ERR_INVALID, "unknown mode"),
+        ({"mode": nat.LINEAR_RESIDUAL}, nat.ERR_INVALID, "one segment"),
+        ({"mode": nat.LINEAR_SWIGLU}, nat.ERR_INVALID, "two segments"),
+        ({"x": (1 << 20) + 8}, nat.ERR_INVALID, "x must be"),
+        ({"x_stride": 2047}, nat.ERR_INVALID, "x_stride"),
+        ({"num_segments": 0}, nat.ERR_INVALID, "num_segments"),
+    ],
+)
+def test_linear_validation(native_lib, over, code, text):
+    p = _linear_params()
+    for k, v in over.items():
+        setattr(p, k, v)
+    assert native_lib.aicas_decode_linear(ctypes.byref(p), None, 0, None) == code
+    assert text in nat.last_error()
+    assert native_lib.aicas_linear_workspace_bytes(ctypes.byref(p)) == 0
+
+
+def test_linear_needs_its_workspace(native_lib):
+    p = _linear_params()
+    assert native_lib.aicas_decode_linear(ctypes.byref(p), None, 0, None) == nat.ERR_WORKSPACE
+    assert "zero-initialised workspace" in nat.last_error()
+    p.seg[1].weight_stride = 2044
+    assert native_lib.aicas_decode_linear(ctypes.byref(p), None, 0, None) == nat.ERR_INVALID
+    assert "segment 1" in nat.last_error()

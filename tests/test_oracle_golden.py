@@ -127,3 +127,43 @@ def test_merge_of_sharded_partials_equals_full():
     po, pl = oa.sharded_decode_partials(q.numpy(), k.numpy(), v.numpy(), wl.SCALE_TEXT, 2, 4)
     m = pl.max(0)
     np.testing.assert_allclose(m + np.log2(np.exp2(pl - m).sum(0)), lse, rtol=0, atol=1e-10)
+
+
+def test_decode_linear_oracle_against_hf_modules():
+    """oracle.decode_linear restates Qwen3VLTextRMSNorm and Qwen3VLTextMLP:
+    same values as the HF modules run in bf16 on CPU (the norm's fp32 reduction
+    order and the CPU GEMM's accumulation may move a value by one unit in the
+    last place)."""
+    import torch
+    from transformers.models.qwen3_vl.configuration_qwen3_vl import Qwen3VLTextConfig
+    from transformers.models.qwen3_vl.modeling_qwen3_vl import Qwen3VLTextMLP, Qwen3VLTextRMSNorm
+
+    from oracle import decode_linear as odl
+
+    g = torch.Generator().manual_seed(5)
+    R, K, N = 6, 256, 384
+    x = torch.randn(R, K, generator=g).to(torch.bfloat16)
+    norm = Qwen3VLTextRMSNorm(K, eps=1e-6).to(torch.bfloat16)
+    with torch.no_grad():
+        norm.weight.copy_((1 + 0.1 * torch.randn(K, generator=g)).to(torch.bfloat16))
+        hf_norm = norm(x).float().numpy()
+    f32 = lambda t: t.float().numpy()  # noqa: E731
+    ours = odl.rms_norm_rows(f32(x), f32(norm.weight.detach()), 1e-6, "bf16")
+    assert (ours == hf_norm).mean() > 0.99
+    assert np.abs(ours - hf_norm).max() <= 2 ** -7 * np.abs(hf_norm).max()
+
+    cfg = Qwen3VLTextConfig(hidden_size=K, intermediate_size=N, hidden_act="silu")
+    mlp = Qwen3VLTextMLP(cfg).to(torch.bfloat16)
+    with torch.no_grad():
+        for lin in (mlp.gate_proj, mlp.up_proj):
+            lin.weight.copy_((torch.randn(N, K, generator=g) / K ** 0.5).to(torch.bfloat16))
+        xn = norm(x)
+        hf_h = mlp.act_fn(mlp.gate_proj(xn)) * mlp.up_proj(xn)
+    (h,) = odl.decode_linear(f32(x), [f32(mlp.gate_proj.weight.detach()), f32(mlp.up_proj.weight.detach())],
+                             norm_weight=f32(norm.weight.detach()), eps=1e-6, swiglu=True)
+    from oracle.rope import round_to
+
+    h = round_to(h.astype(np.float32), "bf16")
+    hf_h = hf_h.float().numpy()
+    assert np.abs(h - hf_h).max() <= 2 ** -6 * np.abs(hf_h).max()
+    assert (h == hf_h).mean() > 0.9
