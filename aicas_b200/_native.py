@@ -41,6 +41,7 @@ LINEAR_STORE = 0
 LINEAR_RESIDUAL = 1
 LINEAR_SWIGLU = 2
 LINEAR_NO_PDL = 1
+LINEAR_STREAM_K = 2
 
 _i64 = ctypes.c_int64
 _i32 = ctypes.c_int32
@@ -124,6 +125,7 @@ class LinearParams(ctypes.Structure):
         ("residual", _vp), ("residual_stride", _i64),
         ("num_segments", _i32), ("seg", LinearSegment * LINEAR_MAX_SEGMENTS),
         ("dtype", _i32), ("flags", _i32),
+        ("sumsq_out", _vp), ("x_sumsq", _vp),
     ]
 
 

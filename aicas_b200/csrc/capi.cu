@@ -286,6 +286,17 @@ int check_linear(const aicas_linear_params* p) {
     if (writes && p->batch > 1 && g.out_stride < g.rows)
       return fail(AICAS_ERR_INVALID, "segment %d: out_stride must be >= rows", j);
   }
+  if (p->sumsq_out != nullptr) {
+    if (p->num_segments != 1 || p->mode == AICAS_LINEAR_SWIGLU)
+      return fail(AICAS_ERR_INVALID, "sumsq_out takes one segment and a store or residual epilogue");
+    if ((reinterpret_cast<uintptr_t>(p->sumsq_out) & 3u) != 0)
+      return fail(AICAS_ERR_INVALID, "sumsq_out must be 4-byte aligned");
+  }
+  if (p->x_sumsq != nullptr) {
+    if (p->norm_weight == nullptr) return fail(AICAS_ERR_INVALID, "x_sumsq needs norm_weight");
+    if ((reinterpret_cast<uintptr_t>(p->x_sumsq) & 3u) != 0)
+      return fail(AICAS_ERR_INVALID, "x_sumsq must be 4-byte aligned");
+  }
   if (p->mode == AICAS_LINEAR_RESIDUAL) {
     if (p->residual == nullptr || (reinterpret_cast<uintptr_t>(p->residual) & 1u) != 0)
       return fail(AICAS_ERR_INVALID, "the residual epilogue needs a 2-byte aligned residual");

@@ -122,17 +122,23 @@ class GraphGreedyDecoder:
 
     def _step_fused(self, st: dict) -> None:
         """The step with every product on :func:`aicas_b200.ops.decode_linear`:
-        per layer, RMSNorm + q/k/v, the fused q/k norm + RoPE + append, decode
-        attention, o_proj + residual, RMSNorm + gate/up + SiLU*up, down_proj +
-        residual; then the final RMSNorm + LM head."""
+        per layer, q/k/v, the fused q/k norm + RoPE + append, decode attention,
+        o_proj + residual, gate/up + SiLU*up, down_proj + residual; then the LM
+        head.  Each residual product also writes the sums of squares of the
+        residual stream's rows (``sumsq_out``), so the following product
+        normalises its input from those statistics (``x_sumsq``) without a pass
+        over x; only layer 0 computes them from the embedding itself."""
         B, D = st["tok"].shape[0], self.head_dim
         x = self.lm.embed_tokens(st["tok"]).view(B, -1)
+        ss = torch.empty(B, dtype=torch.float32, device=x.device)  # row sums of squares of x
         cos, sin = self.lm.rotary_emb(x.view(B, 1, -1), st["pos"])
-        for i, layer in enumerate(self.lm.layers):
+        layers = self.lm.layers
+        for i, layer in enumerate(layers):
             attn, mlp = layer.self_attn, layer.mlp
             ln1, ln2 = layer.input_layernorm, layer.post_attention_layernorm
             q, k, v = ops.decode_linear(x, (attn.q_proj.weight, attn.k_proj.weight, attn.v_proj.weight),
-                                        norm_weight=ln1.weight, eps=ln1.variance_epsilon)
+                                        norm_weight=ln1.weight, eps=ln1.variance_epsilon,
+                                        x_sumsq=ss if i > 0 else None)
             kc, vc = st["caches"][i]
             qr = ops.rope_kv_append(q.view(B, 1, self.hq, D).transpose(1, 2), k.view(B, 1, self.hkv, D).transpose(1, 2),
                                     v.view(B, 1, self.hkv, D).transpose(1, 2), cos, sin, kc, vc, st["lens"],
@@ -140,12 +146,12 @@ class GraphGreedyDecoder:
                                     k_norm_weight=attn.k_norm.weight, eps=attn.q_norm.variance_epsilon)
             o = ops.gqa_decode_attention(qr, kc, vc, sm_scale=attn.scaling, num_key_value_groups=self.group,
                                          kv_lens=st["lens_next"])
-            ops.decode_linear(o.reshape(B, self.hq * D), attn.o_proj.weight, residual=x, out=x)
+            ops.decode_linear(o.reshape(B, self.hq * D), attn.o_proj.weight, residual=x, out=x, sumsq_out=ss)
             h = ops.decode_linear(x, (mlp.gate_proj.weight, mlp.up_proj.weight), norm_weight=ln2.weight,
-                                  eps=ln2.variance_epsilon, swiglu=True)
-            ops.decode_linear(h, mlp.down_proj.weight, residual=x, out=x)
+                                  eps=ln2.variance_epsilon, x_sumsq=ss, swiglu=True)
+            ops.decode_linear(h, mlp.down_proj.weight, residual=x, out=x, sumsq_out=ss)
         logits = ops.decode_linear(x, self.lm_head.weight, norm_weight=self.lm.norm.weight,
-                                   eps=self.lm.norm.variance_epsilon)
+                                   eps=self.lm.norm.variance_epsilon, x_sumsq=ss)
         self._advance(st, logits)
 
     def _step_modules(self, st: dict) -> None:

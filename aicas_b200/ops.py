@@ -519,7 +519,10 @@ def decode_linear(
     residual: torch.Tensor | None = None,
     swiglu: bool = False,
     out: torch.Tensor | Sequence[torch.Tensor] | None = None,
+    sumsq_out: torch.Tensor | None = None,
+    x_sumsq: torch.Tensor | None = None,
     pdl: bool = True,
+    stream_k: bool = False,
 ):
     """Weight-streaming products for the few rows of a decode step, on the
     tensor cores, with the neighbouring elementwise work fused:
@@ -536,9 +539,19 @@ def decode_linear(
     * ``swiglu=True`` with ``weights=(gate, up)``: returns
       ``silu(x' Wg^T) * (x' Wu^T)`` (gate_up_silu_matvec_kernel :174-220,
       rounded as HF Qwen3VLTextMLP rounds).
+    * ``sumsq_out`` ``[R]`` fp32 (one weight, no swiglu): receives the sum of
+      squares of each row of the rounded output, the statistics of the next
+      RMSNorm.  A later call passes it as ``x_sumsq`` together with
+      ``norm_weight``: x then goes by TMA straight into the tensor cores'
+      operand layout and is normalised there, with no statistics pass over x.
 
     Every tensor is fp16 or bf16 of one dtype with unit stride on the last
     dimension.  Inputs the kernel cannot take raise ``ValueError``.
+
+    ``stream_k=True`` splits K over all SMs in stream-K ranges even when the
+    output has fewer 128-feature tiles than SMs (where the default is one CTA
+    cluster per tile, reducing through distributed shared memory); ``pdl=False``
+    launches without programmatic dependent launch.  Both only change timing.
     """
     single = isinstance(weights, torch.Tensor)
     ws_list = [weights] if single else list(weights)
@@ -565,6 +578,16 @@ def decode_linear(
         raise ValueError("residual takes exactly one weight")
     if norm_weight is not None and (norm_weight.shape != (K,) or not norm_weight.is_contiguous()):
         raise ValueError(f"norm_weight must be a contiguous [{K}] tensor")
+    if sumsq_out is not None:
+        if swiglu or len(ws_list) != 1:
+            raise ValueError("sumsq_out takes exactly one weight and no swiglu")
+        if sumsq_out.shape != (R,) or sumsq_out.dtype != torch.float32 or not sumsq_out.is_cuda:
+            raise ValueError(f"sumsq_out must be a CUDA fp32 [{R}] tensor")
+    if x_sumsq is not None:
+        if norm_weight is None:
+            raise ValueError("x_sumsq needs norm_weight")
+        if x_sumsq.shape != (R,) or x_sumsq.dtype != torch.float32 or not x_sumsq.is_cuda:
+            raise ValueError(f"x_sumsq must be a CUDA fp32 [{R}] tensor")
     n_out = 1 if swiglu else len(ws_list)
     rows = [w.shape[0] for w in ws_list]
     if out is None:
@@ -592,7 +615,8 @@ def decode_linear(
         o = outs[min(i, n_out - 1)]
         p.seg[i].out, p.seg[i].out_stride = o.data_ptr(), o.stride(0)
     p.dtype = _LINEAR_DTYPES[x.dtype]
-    p.flags = 0 if pdl else nat.LINEAR_NO_PDL
+    p.flags = (0 if pdl else nat.LINEAR_NO_PDL) | (nat.LINEAR_STREAM_K if stream_k else 0)
+    p.sumsq_out, p.x_sumsq = _ptr(sumsq_out), _ptr(x_sumsq)
     device = x.device
 
     def run():

@@ -263,6 +263,8 @@ AICAS_API int aicas_rope_kv_append(const aicas_rope_append_params* p, void* stre
 #define AICAS_LINEAR_RESIDUAL 1 /* out = residual + round(X' W^T) (one segment; out may alias residual) */
 #define AICAS_LINEAR_SWIGLU 2   /* out = silu(round(X' Wg^T)) * round(X' Wu^T): segment 0 gate, 1 up */
 #define AICAS_LINEAR_NO_PDL 1   /* flags: launch without programmatic dependent launch */
+#define AICAS_LINEAR_STREAM_K 2 /* flags: split K across all SMs with stream-K ranges even when the
+                                   output has few tiles (default there: a CTA cluster per tile) */
 
 typedef struct aicas_linear_segment {
   const void* weight;    /* [rows, in_features] with weight_stride elements between rows */
@@ -288,6 +290,12 @@ typedef struct aicas_linear_params {
   aicas_linear_segment seg[AICAS_LINEAR_MAX_SEGMENTS];
   int32_t dtype;         /* AICAS_DTYPE_F16 or AICAS_DTYPE_BF16, shared by every tensor */
   int32_t flags;         /* AICAS_LINEAR_NO_PDL */
+  float* sumsq_out;       /* optional (one segment, STORE or RESIDUAL): [batch] fp32 receives the
+                             sum of squares of each row of the (rounded) output -- the statistics
+                             of the next RMSNorm, written by the last CTA to finish */
+  const float* x_sumsq;   /* optional with norm_weight: [batch] fp32 sums of squares of the rows of x
+                             (a previous call's sumsq_out); x is then copied by TMA and normalised in
+                             shared memory instead of re-reading it for the statistics */
 } aicas_linear_params;
 
 /* Bytes of zero-initialised workspace aicas_decode_linear needs (tile counters

@@ -209,19 +209,29 @@ def _linear_params(R=8, K=2048, rows=(2048, 1024, 1024), mode=nat.LINEAR_STORE) 
 
 
 def test_linear_workspace_size(native_lib):
-    # stream-K over (tile, 64-K block) units, one CTA per SM (148 without a GPU):
-    # a fixed 64 KiB region of tile counters + two fp32 partial slots per CTA
-    p = _linear_params()
-    grid = min(148, 32 * 32)
-    assert native_lib.aicas_linear_workspace_bytes(ctypes.byref(p)) == 65536 + 2 * grid * 16 * 128 * 4
+    # a fixed 64 KiB region of counters, then (stream-K only) two fp32 partial
+    # slots per CTA, then (sumsq_out only) per-row sums of squares per share.
+    # Fewer tiles than SMs (148 without a GPU): a CTA cluster per tile adds the
+    # partials in shared memory, so no partial slots.
+    base, slot16 = 65536, 16 * 128 * 4
+    p = _linear_params()  # q/k/v: 32 tiles, cluster split
+    assert native_lib.aicas_linear_workspace_bytes(ctypes.byref(p)) == base
+    p.flags = nat.LINEAR_STREAM_K
+    assert native_lib.aicas_linear_workspace_bytes(ctypes.byref(p)) == base + 2 * 148 * slot16
     p = _linear_params(R=20, K=6144, rows=(2048,), mode=nat.LINEAR_RESIDUAL)
     p.residual, p.residual_stride = 9 << 20, 2048
-    assert native_lib.aicas_linear_workspace_bytes(ctypes.byref(p)) == 65536 + 2 * 148 * 32 * 128 * 4
+    assert native_lib.aicas_linear_workspace_bytes(ctypes.byref(p)) == base
+    p.flags = nat.LINEAR_STREAM_K
+    assert native_lib.aicas_linear_workspace_bytes(ctypes.byref(p)) == base + 2 * 148 * 2 * slot16
+    # sumsq_out: 16 tiles x 8 ranks share the sums (128 shares of 32 floats)
+    p.flags = 0
+    p.sumsq_out = 10 << 20
+    assert native_lib.aicas_linear_workspace_bytes(ctypes.byref(p)) == base + 128 * 32 * 4
     p = _linear_params(rows=(6144, 6144), mode=nat.LINEAR_SWIGLU)
-    assert native_lib.aicas_linear_workspace_bytes(ctypes.byref(p)) == 65536 + 2 * 148 * 2 * 16 * 128 * 4
-    p = _linear_params(rows=(151936,))
-    assert native_lib.aicas_linear_workspace_bytes(ctypes.byref(p)) == 65536 + 2 * 148 * 16 * 128 * 4
-    p = _linear_params(rows=(16384 * 128 + 1,))  # more tiles than the counter region holds
+    assert native_lib.aicas_linear_workspace_bytes(ctypes.byref(p)) == base
+    p = _linear_params(rows=(151936,))  # the LM head: 1187 tiles, stream-K
+    assert native_lib.aicas_linear_workspace_bytes(ctypes.byref(p)) == base + 2 * 148 * slot16
+    p = _linear_params(rows=(16383 * 128 + 1,))  # more tiles than the counter region holds
     assert native_lib.aicas_linear_workspace_bytes(ctypes.byref(p)) == 0
     assert "exceed" in nat.last_error()
 

@@ -58,9 +58,12 @@ CASES = [
 
 @pytest.mark.parametrize("R,K,rows", CASES)
 @pytest.mark.parametrize("norm", [False, True])
-def test_store_segments(cuda_device, native_lib, R, K, rows, norm):
+@pytest.mark.parametrize("stream_k", [False, True])
+def test_store_segments(cuda_device, native_lib, R, K, rows, norm, stream_k):
+    """Both partitions: a CTA cluster per tile (the default below 148 tiles)
+    and stream-K ranges over all SMs."""
     x, ws, nw = _data(R, K, rows, torch.bfloat16, cuda_device, seed=R * 7 + K)
-    outs = ops.decode_linear(x, ws, norm_weight=nw if norm else None, eps=1e-6)
+    outs = ops.decode_linear(x, ws, norm_weight=nw if norm else None, eps=1e-6, stream_k=stream_k)
     outs = [outs] if isinstance(outs, torch.Tensor) else list(outs)
     refs = odl.decode_linear(_f32(x), [_f32(w) for w in ws], norm_weight=_f32(nw) if norm else None, eps=1e-6)
     for o, r in zip(outs, refs):
@@ -68,24 +71,55 @@ def test_store_segments(cuda_device, native_lib, R, K, rows, norm):
 
 
 @pytest.mark.parametrize("R,K,N", [(8, 2048, 2048), (8, 6144, 2048), (20, 2048, 1536), (1, 512, 200)])
-def test_residual_in_place(cuda_device, native_lib, R, K, N):
+@pytest.mark.parametrize("stream_k", [False, True])
+def test_residual_in_place(cuda_device, native_lib, R, K, N, stream_k):
     x, (w,), _ = _data(R, K, [N], torch.bfloat16, cuda_device, seed=11 + R)
     res = torch.randn(R, N, generator=torch.Generator().manual_seed(3)).to(torch.bfloat16).to(cuda_device)
     ref = odl.decode_linear(_f32(x), [_f32(w)], residual=_f32(res))[0]
-    y = ops.decode_linear(x, w, residual=res, out=res)
+    y = ops.decode_linear(x, w, residual=res, out=res, stream_k=stream_k)
     assert y.data_ptr() == res.data_ptr()
     _check(res, ref)
 
 
 @pytest.mark.parametrize("R,K,N", [(8, 2048, 6144), (1, 2048, 384), (24, 1024, 1000)])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-def test_swiglu_with_norm(cuda_device, native_lib, R, K, N, dtype):
+@pytest.mark.parametrize("stream_k", [False, True])
+def test_swiglu_with_norm(cuda_device, native_lib, R, K, N, dtype, stream_k):
     x, (wg, wu), nw = _data(R, K, [N, N], dtype, cuda_device, seed=R + N)
-    h = ops.decode_linear(x, (wg, wu), norm_weight=nw, eps=1e-6, swiglu=True)
+    h = ops.decode_linear(x, (wg, wu), norm_weight=nw, eps=1e-6, swiglu=True, stream_k=stream_k)
     name = "bf16" if dtype == torch.bfloat16 else "fp16"
     ref = odl.decode_linear(_f32(x), [_f32(wg), _f32(wu)], norm_weight=_f32(nw), eps=1e-6, swiglu=True,
                             dtype=name)[0]
     _check(h, ref)
+
+
+@pytest.mark.parametrize("R,K,N", [(8, 2048, 2048), (8, 6144, 2048), (32, 1024, 512), (3, 256, 1000)])
+@pytest.mark.parametrize("stream_k", [False, True])
+def test_sumsq_handoff(cuda_device, native_lib, R, K, N, stream_k):
+    """The residual epilogue also returns each output row's sum of squares; the
+    next product normalises its input in shared memory from those statistics
+    and matches the call that computes them from x itself."""
+    h, (w,), _ = _data(R, K, [N], torch.bfloat16, cuda_device, seed=5 + R)
+    g = torch.Generator().manual_seed(6)
+    x = torch.randn(R, N, generator=g).to(torch.bfloat16).to(cuda_device)
+    w2 = (1 + 0.1 * torch.randn(N, generator=g)).to(torch.bfloat16).to(cuda_device)
+    x0 = _f32(x)
+    ss = torch.full((R,), -1.0, device=cuda_device)
+    ops.decode_linear(h, w, residual=x, out=x, sumsq_out=ss, stream_k=stream_k)
+    ref = odl.decode_linear(_f32(h), [_f32(w)], residual=x0)[0]
+    _check(x, ref)
+    xf = _f32(x).astype(np.float64)
+    np.testing.assert_allclose(ss.cpu().numpy(), (xf ** 2).sum(axis=1), rtol=1e-5)
+    # the next product: statistics from sumsq (x by TMA, normalised in place) vs
+    # statistics computed from x by the kernel's own prologue
+    wn = (torch.randn(384, N, generator=g) / N ** 0.5).to(torch.bfloat16).to(cuda_device)
+    a = ops.decode_linear(x, wn, norm_weight=w2, eps=1e-6, x_sumsq=ss, stream_k=stream_k)
+    b = ops.decode_linear(x, wn, norm_weight=w2, eps=1e-6, stream_k=stream_k)
+    refn = odl.decode_linear(_f32(x), [_f32(wn)], norm_weight=_f32(w2), eps=1e-6)[0]
+    _check(a, refn)
+    torch.cuda.synchronize()
+    assert (a != b).float().mean().item() < 0.02
+    assert nat.device_error_flags() == 0
 
 
 def test_lm_head_shape_and_determinism(cuda_device, native_lib):
@@ -122,10 +156,12 @@ def test_graph_capture_of_a_layer_chain(cuda_device, native_lib):
 
     def chain(x):
         q = ops.decode_linear(x, wq, norm_weight=n1)
-        ops.decode_linear(q, wo, residual=x, out=x)
-        h = ops.decode_linear(x, (wg, wu), norm_weight=n2, swiglu=True)
+        ops.decode_linear(q, wo, residual=x, out=x, sumsq_out=ss)
+        h = ops.decode_linear(x, (wg, wu), norm_weight=n2, x_sumsq=ss, swiglu=True)
         ops.decode_linear(h, wd, residual=x, out=x)
         return x
+
+    ss = torch.zeros(R, device=cuda_device)
 
     eager = chain(x0.clone())
     xs = x0.clone()
