@@ -2,6 +2,7 @@
 // with bounded waits, bulk / tensor copies (TMA into this CTA's own shared
 // memory only) and the device-side error word.
 #pragma once
+#include <utility>
 
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -183,6 +184,25 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 // grid on the stream be scheduled before this one ends.
 __device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Launch with programmatic stream serialisation: the kernel may start while
+// the previous kernel on the stream finishes; it calls grid_dependency_wait()
+// before touching anything that kernel writes.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 __device__ __forceinline__ uint32_t lane_id() { return threadIdx.x & 31u; }
 

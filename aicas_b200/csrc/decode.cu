@@ -133,6 +133,10 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kThreads)
     fence_mbar_init();
   }
   __syncthreads();
+  // launched with programmatic dependent launch: set-up above overlaps the
+  // kernel before this one (the query, lengths, cache and workspace come after)
+  if (threadIdx.x == 0) grid_launch_dependents();
+  grid_dependency_wait();
 
   if (warp == C::kWarps) {
     // ------------------------------------------------------------ producer
@@ -502,8 +506,7 @@ static cudaError_t launch_decode_t(const DecodeArgs& a, cudaStream_t st) {
   }
   const long long items = (long long)a.batch * a.hkv * a.max_splits;
   const int grid = (int)(items < per_device ? items : per_device);
-  decode_gqa_kernel<T, D, G><<<grid, C::kThreads, C::kSmemBytes, st>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(decode_gqa_kernel<T, D, G>, dim3(grid), dim3(C::kThreads), C::kSmemBytes, st, a);
 }
 
 template <typename T, int D>

@@ -53,6 +53,10 @@ __global__ void __launch_bounds__(128) rope_append_kernel(const RopeArgs a) {
   const int b = row / a.seq, s = row % a.seq;
   const int slot_head = blockIdx.y * 4 + warp;
   const int nheads = a.hq + 2 * a.hkv;
+  // launched with programmatic dependent launch: the attention that follows
+  // may set up meanwhile; the inputs come from the kernel before this one
+  grid_launch_dependents();
+  grid_dependency_wait();
   if (a.kv_lens_out != nullptr && s == 0 && blockIdx.y == 0 && threadIdx.x == 0)
     a.kv_lens_out[b] = min(max(a.positions[b], 0) + a.seq, a.cap);
   if (slot_head >= nheads) return;
@@ -135,16 +139,13 @@ cudaError_t launch_rope_append(int dtype, int cs_dtype, const RopeArgs& a, cudaS
   const bool f32cs = cs_dtype == AICAS_DTYPE_F32;
   switch (dtype) {
     case AICAS_DTYPE_F32:
-      rope_append_kernel<float, float><<<grid, 128, 0, st>>>(a);
-      break;
+      return launch_pdl(rope_append_kernel<float, float>, grid, dim3(128), 0, st, a);
     case AICAS_DTYPE_F16:
-      if (f32cs) rope_append_kernel<__half, float><<<grid, 128, 0, st>>>(a);
-      else rope_append_kernel<__half, __half><<<grid, 128, 0, st>>>(a);
-      break;
+      return f32cs ? launch_pdl(rope_append_kernel<__half, float>, grid, dim3(128), 0, st, a)
+                   : launch_pdl(rope_append_kernel<__half, __half>, grid, dim3(128), 0, st, a);
     case AICAS_DTYPE_BF16:
-      if (f32cs) rope_append_kernel<__nv_bfloat16, float><<<grid, 128, 0, st>>>(a);
-      else rope_append_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, 128, 0, st>>>(a);
-      break;
+      return f32cs ? launch_pdl(rope_append_kernel<__nv_bfloat16, float>, grid, dim3(128), 0, st, a)
+                   : launch_pdl(rope_append_kernel<__nv_bfloat16, __nv_bfloat16>, grid, dim3(128), 0, st, a);
     default:
       return cudaErrorInvalidValue;
   }
