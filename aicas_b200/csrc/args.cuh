@@ -22,6 +22,7 @@ struct DecodeArgs {
   float* ws_lse;          // [B*Hkv, max_splits, G]
   unsigned int* ws_count; // [B*Hkv] split counters (null: no split-KV workspace)
   unsigned int* ws_sched; // [2] work-item counter, finished-CTA counter (with a workspace)
+  int prefetch_first;     // 1: each CTA brings its first item's K/V range into L2 before the dependency wait
   unsigned int* err;      // device error word
 };
 

@@ -136,6 +136,27 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kThreads)
   // launched with programmatic dependent launch: set-up above overlaps the
   // kernel before this one (the query, lengths, cache and workspace come after)
   if (threadIdx.x == 0) grid_launch_dependents();
+  if (a.prefetch_first && threadIdx.x == C::kWarps * 32) {
+    // this CTA's first item is item blockIdx.x (see the claim loop below); its
+    // split covers the same tokens whatever the lengths turn out to be, so its
+    // K/V can be brought into L2 while the kernel before this one finishes
+    const int bh = (int)blockIdx.x % (a.batch * a.hkv), split = (int)blockIdx.x / (a.batch * a.hkv);
+    const int b = bh / a.hkv, kvh = bh % a.hkv;
+    const int t0 = split * a.split_tokens;
+    const int ntok = min(a.cap, t0 + a.split_tokens) - t0;
+    if (ntok > 0) {
+      const uint8_t* gk = static_cast<const uint8_t*>(a.k) +
+                          ((int64_t)b * a.k_sb + (int64_t)kvh * a.k_sh + (int64_t)t0 * D) * sizeof(T);
+      const uint8_t* gv = static_cast<const uint8_t*>(a.v) +
+                          ((int64_t)b * a.v_sb + (int64_t)kvh * a.v_sh + (int64_t)t0 * D) * sizeof(T);
+      const uint32_t bytes = (uint32_t)ntok * C::kRowBytes;
+      for (uint32_t off = 0; off < bytes; off += 65536u) {
+        const uint32_t n = bytes - off < 65536u ? bytes - off : 65536u;
+        bulk_prefetch_l2(gk + off, n);
+        bulk_prefetch_l2(gv + off, n);
+      }
+    }
+  }
   grid_dependency_wait();
 
   if (warp == C::kWarps) {
@@ -145,6 +166,7 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kThreads)
       uint32_t g = 0;       // K/V tiles issued so far (ring position)
       uint32_t qi = 0;      // items announced so far (queue position)
       int k = 0;            // round-robin position (static scheduling)
+      bool first_claim = true;
       bool ok = true;
       for (;;) {
         // claim the next non-empty item (or run out)
@@ -153,7 +175,9 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kThreads)
         for (;;) {
           int cand;
           if (dynamic) {
-            cand = (int)atomicAdd(next_item, 1u);
+            // the first item is this CTA's own index; the counter hands out the rest
+            cand = first_claim ? (int)blockIdx.x : (int)gridDim.x + (int)atomicAdd(next_item, 1u);
+            first_claim = false;
           } else {
             cand = (int)blockIdx.x + k * (int)gridDim.x;
             ++k;
@@ -506,7 +530,12 @@ static cudaError_t launch_decode_t(const DecodeArgs& a, cudaStream_t st) {
   }
   const long long items = (long long)a.batch * a.hkv * a.max_splits;
   const int grid = (int)(items < per_device ? items : per_device);
-  return launch_pdl(decode_gqa_kernel<T, D, G>, dim3(grid), dim3(C::kThreads), C::kSmemBytes, st, a);
+  // the first items' K/V into L2 ahead of the dependency wait, when they fit
+  // comfortably (a larger prefetch would evict itself before it is read)
+  DecodeArgs b = a;
+  const long long first_bytes = (long long)grid * (a.split_tokens < a.cap ? a.split_tokens : a.cap) * 2 * C::kRowBytes;
+  b.prefetch_first = (a.ws_sched != nullptr && first_bytes <= (64ll << 20)) ? 1 : 0;
+  return launch_pdl(decode_gqa_kernel<T, D, G>, dim3(grid), dim3(C::kThreads), C::kSmemBytes, st, b);
 }
 
 template <typename T, int D>
