@@ -477,6 +477,60 @@ def time_varlen(args, world, device, peaks) -> dict:
             "config": f"32 images, grids U[16,64]^2, T={int(cu[-1])}, H16 D64, non-causal", "scaling": "weak (replicas)"}
 
 
+def run_products(args, world, device, peaks) -> dict:
+    """The weight-streaming side of one batch-8 decode step of Qwen3-VL-2B on
+    aicas_decode_linear, captured in one CUDA graph: 28 layers x (RMSNorm +
+    q/k/v, o_proj + residual, RMSNorm + gate/up + SiLU*up, down_proj +
+    residual) with distinct random weights per layer, then RMSNorm + the LM
+    head.  Weights (3.44 GB a step) are far larger than L2, so every step
+    streams them from HBM; achieved = weight bytes / step time."""
+    from aicas_b200 import ops
+
+    R, H, I, V, L = 8, 2048, 6144, 151936, LAYERS
+    g = torch.Generator(device=device).manual_seed(0)
+
+    def w(n, k):
+        return (torch.randn(n, k, device=device, generator=g) / k ** 0.5).to(torch.bfloat16)
+
+    layers = [(w(2048, H), w(1024, H), w(1024, H), w(H, 2048), w(I, H), w(I, H), w(H, I)) for _ in range(L)]
+    lm = w(V, H)
+    nw = (1 + 0.1 * torch.randn(H, device=device, generator=g)).to(torch.bfloat16)
+    x0 = torch.randn(R, H, device=device, generator=g).to(torch.bfloat16)
+    x, ss = x0.clone(), torch.zeros(R, device=device)
+    wbytes = sum(t.numel() * 2 for lw in layers for t in lw) + lm.numel() * 2
+
+    def step():
+        x.copy_(x0)
+        for i, (wq, wk, wv, wo, wg, wu, wd) in enumerate(layers):
+            q, _, _ = ops.decode_linear(x, (wq, wk, wv), norm_weight=nw, x_sumsq=ss if i else None)
+            ops.decode_linear(q, wo, residual=x, out=x, sumsq_out=ss)
+            h = ops.decode_linear(x, (wg, wu), norm_weight=nw, x_sumsq=ss, swiglu=True)
+            ops.decode_linear(h, wd, residual=x, out=x, sumsq_out=ss)
+        return ops.decode_linear(x, lm, norm_weight=nw, x_sumsq=ss)
+
+    s = torch.cuda.Stream(device)
+    s.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(s):
+        step()
+    torch.cuda.current_stream(device).wait_stream(s)
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        step()
+    ms = _time_calls(graph.replay, 10, 3, world, device)
+    lm_ms = _time_calls(lambda: ops.decode_linear(x, lm, norm_weight=nw, x_sumsq=ss), 10, 3, world, device)
+    del graph
+    gbs = wbytes / (ms * 1e-3) / 1e9
+    lm_gbs = lm.numel() * 2 / (lm_ms * 1e-3) / 1e9
+    return {"value": round(world * gbs, 1), "unit": "GB/s", "ms_per_step": round(ms, 4),
+            "per_gpu_gbs": round(gbs, 1), "frac_of_hbm": round(gbs / peaks["hbm_gbs"], 4),
+            "weight_bytes_per_step": wbytes, "gpu_launches_per_step": 4 * L + 1,
+            "lm_head": {"ms": round(lm_ms, 4), "gbs": round(lm_gbs, 1),
+                        "frac_of_hbm": round(lm_gbs / peaks["hbm_gbs"], 4)},
+            "config": "batch 8, Qwen3-VL-2B text decoder products (28 layers + LM head), bf16, random weights",
+            "scaling": "weak (replicas)"}
+
+
 # ------------------------------------------------------------------ CPU (reference) path
 
 
@@ -593,7 +647,7 @@ def _main(out: "_JsonStdout", argv=None) -> int:
     ap.add_argument("--no-e2e", dest="e2e", action="store_false", help="skip the end-to-end host-buffer measurement")
     ap.add_argument("--no-generate", dest="generate", action="store_false",
                     help="skip the end-to-end greedy generate on the random-init Qwen3-VL-2B-shaped model")
-    ap.add_argument("--only", choices=["decode", "split_kv", "prefill", "vit", "generate"], default=None,
+    ap.add_argument("--only", choices=["decode", "split_kv", "prefill", "vit", "products", "generate"], default=None,
                     help="run one workload (profiling)")
     ap.add_argument("--layers", type=int, default=LAYERS, help="decode layers per step (28 = Qwen3-VL-2B)")
     args = ap.parse_args(argv)
@@ -627,6 +681,8 @@ def _main(out: "_JsonStdout", argv=None) -> int:
         result["split_kv_cfg5"] = run_split_kv(args, world, rank, device)
     if args.secondary and only in (None, "prefill", "vit"):
         result.update(run_fmha_secondary(args, world, device, peaks, only))
+    if args.secondary and only in (None, "products"):
+        result["decode_products"] = run_products(args, world, device, peaks)
     if world == 1 and ((args.generate and only is None) or only == "generate"):
         result["generate_cfg4"] = run_generate(device)
     line = None
