@@ -34,6 +34,7 @@ CAP_VARLEN_TCGEN05 = 8
 CAP_ROPE_APPEND = 16
 CAP_PEER_EXCHANGE = 32
 CAP_DECODE_LINEAR = 64
+CAP_VISION_ROPE = 128
 
 LINEAR_MAX_SEGMENTS = 4
 LINEAR_MAX_ROWS = 32
@@ -114,6 +115,15 @@ class RopeAppendParams(ctypes.Structure):
     ]
 
 
+class VisionRopeParams(ctypes.Structure):
+    _fields_ = [
+        ("q_in", _vp), ("k_in", _vp), ("q_out", _vp), ("k_out", _vp), ("cos", _vp), ("sin", _vp),
+        ("qi_stride_t", _i64), ("qi_stride_h", _i64), ("ki_stride_t", _i64), ("ki_stride_h", _i64),
+        ("qo_stride_t", _i64), ("qo_stride_h", _i64), ("ko_stride_t", _i64), ("ko_stride_h", _i64),
+        ("cs_stride_t", _i64), ("tokens", _i32), ("heads", _i32), ("head_dim", _i32), ("dtype", _i32),
+    ]
+
+
 class LinearSegment(ctypes.Structure):
     _fields_ = [("weight", _vp), ("weight_stride", _i64), ("out", _vp), ("out_stride", _i64), ("rows", _i32)]
 
@@ -144,6 +154,7 @@ EXPORTS = {
     "aicas_prefill_gqa_causal": (ctypes.c_int, [ctypes.POINTER(FmhaParams), _vp]),
     "aicas_varlen_attention": (ctypes.c_int, [ctypes.POINTER(FmhaParams), _vp]),
     "aicas_rope_kv_append": (ctypes.c_int, [ctypes.POINTER(RopeAppendParams), _vp]),
+    "aicas_vision_rope": (ctypes.c_int, [ctypes.POINTER(VisionRopeParams), _vp]),
     "aicas_linear_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(LinearParams)]),
     "aicas_decode_linear": (ctypes.c_int, [ctypes.POINTER(LinearParams), _vp, ctypes.c_size_t, _vp]),
     "aicas_version": (ctypes.c_char_p, []),

@@ -26,6 +26,17 @@ struct DecodeArgs {
   unsigned int* err;      // device error word
 };
 
+struct VisionRopeArgs {
+  const void* q_in;
+  const void* k_in;
+  void* q_out;
+  void* k_out;
+  const float* cos;  // [T, D] fp32
+  const float* sin;
+  int64_t qi_st, qi_sh, ki_st, ki_sh, qo_st, qo_sh, ko_st, ko_sh, cs_st;
+  int tokens, heads, hd;
+};
+
 struct RopeArgs {
   const void* q_in;
   void* q_out;

@@ -18,6 +18,8 @@ cudaError_t launch_decode(int dtype, int head_dim, int group, const DecodeArgs& 
 int decode_tile_for(int dtype, int head_dim);
 struct RopeArgs;
 cudaError_t launch_rope_append(int dtype, int cs_dtype, const RopeArgs& a, cudaStream_t st);
+struct VisionRopeArgs;
+cudaError_t launch_vision_rope(int dtype, const VisionRopeArgs& a, int sms, cudaStream_t st);
 struct MergeArgs;
 cudaError_t launch_merge(int dtype, const MergeArgs& a, cudaStream_t st);
 struct ExchangeArgs;
@@ -312,7 +314,7 @@ const char* aicas_version(void) { return "aicas_b200 0.1.0 sm_100a abi 1"; }
 
 uint32_t aicas_capabilities(void) {
   return AICAS_CAP_DECODE | AICAS_CAP_MERGE | AICAS_CAP_ROPE_APPEND | AICAS_CAP_PEER_EXCHANGE |
-         AICAS_CAP_DECODE_LINEAR | aicas::fmha_capabilities();
+         AICAS_CAP_DECODE_LINEAR | AICAS_CAP_VISION_ROPE | aicas::fmha_capabilities();
 }
 
 const char* aicas_last_error(void) { return g_err; }
@@ -537,6 +539,51 @@ int aicas_varlen_attention(const aicas_fmha_params* p, void* stream) {
   int rc = check_fmha(p, true);
   if (rc != AICAS_OK) return rc;
   return aicas::run_fmha(p, /*varlen=*/true, static_cast<cudaStream_t>(stream), device_error_word(), g_err, sizeof(g_err));
+}
+
+int aicas_vision_rope(const aicas_vision_rope_params* p, void* stream) {
+  if (p == nullptr) return fail(AICAS_ERR_INVALID, "params is NULL");
+  if (p->dtype != AICAS_DTYPE_F16 && p->dtype != AICAS_DTYPE_BF16)
+    return fail(AICAS_ERR_UNSUPPORTED, "vision RoPE needs fp16 or bf16 q/k (dtype %d)", p->dtype);
+  if (p->tokens < 0 || p->heads <= 0 || p->head_dim <= 0)
+    return fail(AICAS_ERR_INVALID, "tokens=%d heads=%d head_dim=%d", p->tokens, p->heads, p->head_dim);
+  if (p->head_dim % 16 != 0 || p->head_dim > 256)
+    return fail(AICAS_ERR_UNSUPPORTED, "vision RoPE needs head_dim a multiple of 16 up to 256 (got %d)", p->head_dim);
+  if (p->tokens == 0) return AICAS_OK;
+  if (p->q_in == nullptr || p->k_in == nullptr || p->q_out == nullptr || p->k_out == nullptr || p->cos == nullptr ||
+      p->sin == nullptr)
+    return fail(AICAS_ERR_INVALID, "q_in, k_in, q_out, k_out, cos and sin must be set");
+  if (!aligned16(p->q_in) || !aligned16(p->k_in) || !aligned16(p->q_out) || !aligned16(p->k_out) ||
+      !aligned16(p->cos) || !aligned16(p->sin))
+    return fail(AICAS_ERR_INVALID, "device pointers must be 16-byte aligned");
+  const int64_t st16[] = {p->qi_stride_t, p->qi_stride_h, p->ki_stride_t, p->ki_stride_h,
+                          p->qo_stride_t, p->qo_stride_h, p->ko_stride_t, p->ko_stride_h};
+  for (int64_t s : st16)
+    if (s < 0 || !stride_ok(s, 2)) return fail(AICAS_ERR_INVALID, "q/k strides must be non-negative multiples of 8");
+  if (p->cs_stride_t < p->head_dim || (p->cs_stride_t & 3) != 0)
+    return fail(AICAS_ERR_INVALID, "cos/sin row stride must be >= head_dim and a multiple of 4");
+  aicas::VisionRopeArgs a;
+  a.q_in = p->q_in;
+  a.k_in = p->k_in;
+  a.q_out = p->q_out;
+  a.k_out = p->k_out;
+  a.cos = p->cos;
+  a.sin = p->sin;
+  a.qi_st = p->qi_stride_t;
+  a.qi_sh = p->qi_stride_h;
+  a.ki_st = p->ki_stride_t;
+  a.ki_sh = p->ki_stride_h;
+  a.qo_st = p->qo_stride_t;
+  a.qo_sh = p->qo_stride_h;
+  a.ko_st = p->ko_stride_t;
+  a.ko_sh = p->ko_stride_h;
+  a.cs_st = p->cs_stride_t;
+  a.tokens = p->tokens;
+  a.heads = p->heads;
+  a.hd = p->head_dim;
+  const cudaError_t e = aicas::launch_vision_rope(p->dtype, a, sm_count(), static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "vision RoPE launch");
+  return AICAS_OK;
 }
 
 size_t aicas_linear_workspace_bytes(const aicas_linear_params* p) {

@@ -109,14 +109,18 @@ def build_random_model(config, dtype: torch.dtype, device: torch.device | str, s
 def set_attention(model, which: str) -> None:
     """Point the four config objects the patch entry point mutates at
     ``which``: "sdpa" for the unpatched baseline, "aicas" for this backend
-    (through :func:`install_qwen3vl_triton_attention`)."""
+    (through :func:`install_qwen3vl_triton_attention`, with the vision QKV
+    split + RoPE fused into one kernel)."""
+    from .vision import remove_vision_rope_fusion
+
     if which == "aicas":
-        state = install_qwen3vl_triton_attention(model)
+        state = install_qwen3vl_triton_attention(model, fuse_vision_rope=True)
         if not state["triton_available"]:
             raise RuntimeError("the aicas_b200 native library is not loadable; the patched model cannot run")
         return
     if which != "sdpa":
         raise ValueError(f"unknown attention implementation {which!r}")
+    remove_vision_rope_fusion(model)
     base = getattr(model, "model", None)
     for cfg in (
         getattr(getattr(base, "visual", None), "config", None),

@@ -631,3 +631,53 @@ def decode_linear(
     if R > 0:
         _call_in_device(device, run)
     return outs[0] if (single or swiglu) else tuple(outs)
+
+
+# ---------------------------------------------------------------------- vision RoPE
+
+
+def vision_rope(query: torch.Tensor, key: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor):
+    """HF ``apply_rotary_pos_emb_vision(q, k, cos, sin)`` (transformers
+    models/qwen3_vl/modeling_qwen3_vl.py:131-142) in one kernel, bit-identical:
+    q/k ``[T, H, D]`` fp16/bf16 (any strides with a unit last one, e.g. views
+    of the packed qkv projection ``[T, 3, H, D]``), cos/sin ``[T, D]`` (used
+    as fp32, as HF upcasts them).
+    Returns new contiguous ``(q_rot, k_rot)``."""
+    _reject_grad(query, key)
+    if not all(t.is_cuda for t in (query, key, cos, sin)):
+        raise ValueError("vision_rope needs CUDA tensors")
+    if query.ndim != 3 or key.shape != query.shape:
+        raise ValueError("query and key must be [T, H, D] of one shape")
+    T, H, D = query.shape
+    if query.dtype not in _LINEAR_DTYPES or key.dtype != query.dtype:
+        raise ValueError("vision_rope needs fp16 or bf16 query and key of one dtype")
+    if cos.shape != (T, D) or sin.shape != (T, D) or not (cos.is_floating_point() and sin.is_floating_point()):
+        raise ValueError(f"cos/sin must be floating-point [{T}, {D}]")
+    # HF upcasts cos/sin to fp32 inside apply_rotary_pos_emb_vision (exact for 16-bit values)
+    cos, sin = cos.float(), sin.float()
+    if D % 16 or D > 256:
+        raise ValueError("head_dim must be a multiple of 16 up to 256")
+
+    def ready(t):
+        return t if t.stride(-1) == 1 and _aligned(t, t.stride()[:-1]) else t.contiguous()
+
+    query, key = ready(query), ready(key)
+    cos, sin = cos.contiguous(), sin.contiguous()
+    q_out = torch.empty((T, H, D), dtype=query.dtype, device=query.device)
+    k_out = torch.empty_like(q_out)
+    if T == 0:
+        return q_out, k_out
+    p = nat.VisionRopeParams()
+    p.q_in, p.k_in, p.q_out, p.k_out = query.data_ptr(), key.data_ptr(), q_out.data_ptr(), k_out.data_ptr()
+    p.cos, p.sin, p.cs_stride_t = cos.data_ptr(), sin.data_ptr(), cos.stride(0)
+    p.qi_stride_t, p.qi_stride_h = query.stride(0), query.stride(1)
+    p.ki_stride_t, p.ki_stride_h = key.stride(0), key.stride(1)
+    p.qo_stride_t, p.qo_stride_h = q_out.stride(0), q_out.stride(1)
+    p.ko_stride_t, p.ko_stride_h = k_out.stride(0), k_out.stride(1)
+    p.tokens, p.heads, p.head_dim, p.dtype = T, H, D, _LINEAR_DTYPES[query.dtype]
+
+    def run():
+        nat.check(nat.lib().aicas_vision_rope(ctypes.byref(p), _stream_handle(query.device)), "aicas_vision_rope")
+
+    _call_in_device(query.device, run)
+    return q_out, k_out

@@ -30,7 +30,11 @@ def _set_attr_if_present(target: Any, attr_name: str, value: str) -> bool:
     return True
 
 
-def install_qwen3vl_triton_attention(model: Any) -> dict[str, Any]:
+def install_qwen3vl_triton_attention(model: Any, fuse_vision_rope: bool = False) -> dict[str, Any]:
+    """``fuse_vision_rope=True`` (an extension; the reference has no such
+    switch) also runs the vision attention's QKV split + RoPE as one kernel
+    (:mod:`aicas_b200.vision`) and adds ``vision_rope_fused`` (modules
+    switched) to the returned dict."""
     attention_registry, mask_registry = _load_attention_registries()
 
     if VISION_BACKEND_KEY not in attention_registry:
@@ -61,7 +65,13 @@ def install_qwen3vl_triton_attention(model: Any) -> dict[str, Any]:
         ),
     }
     available = _native.available()
+    extra = {}
+    if fuse_vision_rope:
+        from .vision import install_vision_rope_fusion
+
+        extra["vision_rope_fused"] = install_vision_rope_fusion(model)
     return {
+        **extra,
         "installed": True,
         "triton_available": available,
         "vision_backend_key": VISION_BACKEND_KEY,

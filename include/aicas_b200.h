@@ -35,6 +35,10 @@
  *                             (InplaceDecodeCacheLayer.update); optional per-head
  *                             RMSNorm as in dujunbaoV1/native_cuda_ops/
  *                             decode_q1_gqa_kernel.cu:376-480
+ *   aicas_vision_rope         HF apply_rotary_pos_emb_vision (transformers
+ *                             models/qwen3_vl/modeling_qwen3_vl.py:131-142) as the
+ *                             vision attention applies it after splitting the
+ *                             packed QKV projection (:205-209), in one kernel
  *   aicas_decode_linear       the decode-side matrix-vector products of
  *                             dujunbaoV1/native_cuda_ops/decode_q1_gqa_kernel.cu:
  *                             rmsnorm_kernel :127-157 (as a fused prologue),
@@ -254,6 +258,25 @@ typedef struct aicas_rope_append_params {
 AICAS_API int aicas_rope_kv_append(const aicas_rope_append_params* p, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* Vision-tower RoPE of q and k (HF apply_rotary_pos_emb_vision), bit-exact.  */
+/* ------------------------------------------------------------------------ */
+typedef struct aicas_vision_rope_params {
+  const void* q_in;         /* [T, H, D] (e.g. views into the packed qkv projection [T, 3, H, D]) */
+  const void* k_in;
+  void* q_out;              /* [T, H, D] rotated (may not alias the inputs) */
+  void* k_out;
+  const float* cos;         /* [T, D] fp32 */
+  const float* sin;         /* [T, D] fp32 */
+  int64_t qi_stride_t, qi_stride_h, ki_stride_t, ki_stride_h;
+  int64_t qo_stride_t, qo_stride_h, ko_stride_t, ko_stride_h;
+  int64_t cs_stride_t;      /* row stride of cos and sin */
+  int32_t tokens, heads, head_dim; /* head_dim a multiple of 16 */
+  int32_t dtype;            /* AICAS_DTYPE_F16 or AICAS_DTYPE_BF16 */
+} aicas_vision_rope_params;
+
+AICAS_API int aicas_vision_rope(const aicas_vision_rope_params* p, void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* Decode-side weight-streaming products: Y = epilogue(X' W^T) for a few rows */
 /* X (the batch of one decode step) on the tensor cores.                      */
 /* ------------------------------------------------------------------------ */
@@ -318,6 +341,7 @@ AICAS_API const char* aicas_version(void);
 #define AICAS_CAP_ROPE_APPEND 16u
 #define AICAS_CAP_PEER_EXCHANGE 32u
 #define AICAS_CAP_DECODE_LINEAR 64u
+#define AICAS_CAP_VISION_ROPE 128u
 AICAS_API uint32_t aicas_capabilities(void);
 
 /* Message of the last failed call on this thread ("" if none). */

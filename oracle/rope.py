@@ -7,6 +7,9 @@ models/qwen3_vl/modeling_qwen3_vl.py):
   * ``apply_rope``          - apply_rotary_pos_emb / rotate_half (:410-432), with the
                               per-op rounding torch applies to 16-bit tensors
   * ``rms_norm_heads``      - Qwen3VLTextRMSNorm (:389-406) applied per head
+  * ``apply_rope_vision``   - apply_rotary_pos_emb_vision (:131-142): the same rotate-half
+                              form in fp32 (each product and the sum rounded as fp32), the
+                              result rounded once to the tensor dtype
 """
 from __future__ import annotations
 
@@ -77,3 +80,14 @@ def rms_norm_heads(x: np.ndarray, weight: np.ndarray, eps: float, dtype: str) ->
     var = (x.astype(np.float64) ** 2).mean(axis=-1, keepdims=True).astype(np.float32)
     y = round_to(x * (np.float32(1.0) / np.sqrt(var + np.float32(eps))).astype(np.float32), dtype)
     return round_to(np.asarray(weight, dtype=np.float32) * y, dtype)
+
+
+def apply_rope_vision(x: np.ndarray, cos: np.ndarray, sin: np.ndarray, dtype: str) -> np.ndarray:
+    """x [T, H, D] (values of ``dtype``), cos/sin [T, D] fp32 -> rotated x as
+    ``dtype`` values in float32: (x * cos) + (rotate_half(x) * sin) in fp32."""
+    x = np.asarray(x, dtype=np.float32)
+    c = np.asarray(cos, dtype=np.float32)[:, None, :]
+    s = np.asarray(sin, dtype=np.float32)[:, None, :]
+    h = x.shape[-1] // 2
+    rot = np.concatenate([-x[..., h:], x[..., :h]], axis=-1)
+    return round_to((x * c).astype(np.float32) + (rot * s).astype(np.float32), dtype)

@@ -40,7 +40,7 @@ def test_version_and_capabilities(native_lib):
     assert v.startswith("aicas_b200 ") and "sm_100a" in v
     caps = nat.capabilities()
     assert caps & nat.CAP_DECODE and caps & nat.CAP_MERGE and caps & nat.CAP_ROPE_APPEND
-    assert caps & nat.CAP_PEER_EXCHANGE and caps & nat.CAP_DECODE_LINEAR
+    assert caps & nat.CAP_PEER_EXCHANGE and caps & nat.CAP_DECODE_LINEAR and caps & nat.CAP_VISION_ROPE
 
 
 STRUCTS = {
@@ -51,6 +51,7 @@ STRUCTS = {
     "aicas_exchange_params": nat.ExchangeParams,
     "aicas_linear_segment": nat.LinearSegment,
     "aicas_linear_params": nat.LinearParams,
+    "aicas_vision_rope_params": nat.VisionRopeParams,
 }
 
 
@@ -266,3 +267,17 @@ def test_linear_needs_its_workspace(native_lib):
     p.seg[1].weight_stride = 2044
     assert native_lib.aicas_decode_linear(ctypes.byref(p), None, 0, None) == nat.ERR_INVALID
     assert "segment 1" in nat.last_error()
+
+
+def test_vision_rope_validation(native_lib):
+    p = nat.VisionRopeParams()
+    p.tokens, p.heads, p.head_dim, p.dtype = 8, 4, 64, nat.DTYPE_F32
+    assert native_lib.aicas_vision_rope(ctypes.byref(p), None) == nat.ERR_UNSUPPORTED
+    p.dtype, p.head_dim = nat.DTYPE_BF16, 40
+    assert native_lib.aicas_vision_rope(ctypes.byref(p), None) == nat.ERR_UNSUPPORTED
+    assert "multiple of 16" in nat.last_error()
+    p.head_dim = 64
+    assert native_lib.aicas_vision_rope(ctypes.byref(p), None) == nat.ERR_INVALID
+    assert "must be set" in nat.last_error()
+    p.tokens = 0
+    assert native_lib.aicas_vision_rope(ctypes.byref(p), None) == nat.OK  # nothing to do

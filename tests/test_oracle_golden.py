@@ -167,3 +167,22 @@ def test_decode_linear_oracle_against_hf_modules():
     hf_h = hf_h.float().numpy()
     assert np.abs(h - hf_h).max() <= 2 ** -6 * np.abs(hf_h).max()
     assert (h == hf_h).mean() > 0.9
+
+
+def test_vision_rope_oracle_bit_exact_against_hf():
+    """oracle.rope.apply_rope_vision restates apply_rotary_pos_emb_vision: the
+    same bits as HF's function on CPU (bf16 q/k, fp32 cos/sin)."""
+    import torch
+    from transformers.models.qwen3_vl.modeling_qwen3_vl import apply_rotary_pos_emb_vision
+
+    g = torch.Generator().manual_seed(11)
+    T, H, D = 37, 4, 64
+    q = torch.randn(T, H, D, generator=g).to(torch.bfloat16)
+    k = torch.randn(T, H, D, generator=g).to(torch.bfloat16)
+    freqs = torch.randn(T, D // 2, generator=g) * 3
+    emb = torch.cat((freqs, freqs), dim=-1)
+    cos, sin = emb.cos(), emb.sin()
+    hq, hk = apply_rotary_pos_emb_vision(q, k, cos, sin)
+    for x, ref in ((q, hq), (k, hk)):
+        ours = orope.apply_rope_vision(x.float().numpy(), cos.numpy(), sin.numpy(), "bf16")
+        assert np.array_equal(ours, ref.float().numpy())
