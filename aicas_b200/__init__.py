@@ -16,6 +16,7 @@ from .ops import (
     merge_partials,
     rope_kv_append,
     varlen_flash_attention,
+    vision_rope,
 )
 from .patch import install_qwen3vl_triton_attention
 
@@ -38,5 +39,6 @@ __all__ = [
     "rope_kv_append",
     "text_triton_attention",
     "varlen_flash_attention",
+    "vision_rope",
     "vision_triton_attention",
 ]
