@@ -30,7 +30,8 @@
 //   warp 5     TMEM allocation and the MMA-issuing thread
 // Launched with programmatic dependent launch: the weight stream starts before
 // the previous kernel on the stream has finished; only the prologue and the
-// epilogue (activations, outputs, workspace) wait for it.
+// epilogue (activations, outputs, workspace) wait for it.  Dependents are
+// released once a CTA has issued its last product.
 #include <cuda.h>
 
 #include <cstdio>
@@ -421,9 +422,6 @@ __global__ void __launch_bounds__(kThreads, RP == 16 ? 2 : 1) decode_linear_kern
     if (elect_one()) {
       constexpr uint32_t idesc = tc::idesc_f16(kBf16, kTileN, RP, false, false);
       bool ok = mbar_wait(xready, 0, abort_flag, a.err);
-      // the next kernel's CTAs (and their weight traffic) may start once this
-      // CTA's input has landed
-      grid_launch_dependents();
       int portion = 0;
       for (int i = 0; ok && i < n; ++i) {
         const long long u = u0 + i;
@@ -451,6 +449,10 @@ __global__ void __launch_bounds__(kThreads, RP == 16 ? 2 : 1) decode_linear_kern
           ++portion;
         }
       }
+      // the next kernel's CTAs (and their weight traffic) may start once this
+      // CTA has issued its last product: earlier, their L2 prefetch slows this
+      // kernel's own epilogue loads (measured)
+      grid_launch_dependents();
       // every product issued has completed before TMEM is released
       tc::commit(mdone);
       mbar_wait(mdone, 0, nullptr, a.err);
