@@ -86,3 +86,25 @@ def test_attention_switch(tiny, monkeypatch):
     it.set_attention(model, "sdpa")
     with pytest.raises(ValueError):
         it.set_attention(model, "eager")
+
+
+def test_vision_rope_fusion_switch(tiny):
+    """fuse_vision_rope=True puts the fused forward on every vision attention
+    module and reports how many; switching back to SDPA restores Hugging
+    Face's forward (no kernel runs here)."""
+    from transformers.models.qwen3_vl.modeling_qwen3_vl import Qwen3VLVisionAttention
+
+    from aicas_b200 import install_qwen3vl_triton_attention
+    from aicas_b200.vision import fused_vision_attention_forward
+
+    cfg, model = tiny
+    mods = [m for m in model.modules() if isinstance(m, Qwen3VLVisionAttention)]
+    assert len(mods) == cfg.vision_config.depth
+    state = install_qwen3vl_triton_attention(model)
+    assert "vision_rope_fused" not in state and all("forward" not in m.__dict__ for m in mods)
+    state = install_qwen3vl_triton_attention(model, fuse_vision_rope=True)
+    assert state["vision_rope_fused"] == len(mods)
+    assert all(m.forward.__func__ is fused_vision_attention_forward for m in mods)
+    it.set_attention(model, "sdpa")
+    assert all("forward" not in m.__dict__ for m in mods)
+    assert it.attention_in_use(model) == ("sdpa", "sdpa")
