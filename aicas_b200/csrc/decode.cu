@@ -14,7 +14,8 @@
 //     query head);
 //   * a producer warp streams 16 KB K and V tiles with cp.async.bulk (TMA into
 //     this CTA's shared memory, L2 evict-first) into a 3-stage mbarrier ring;
-//   * 4 consumer warps each own a quarter of every tile: 16-byte vector reads
+//   * 8 consumer warps (4 for groups of 4 or more query heads) each own a
+//     slice of every tile: 16-byte vector reads
 //     from shared memory, a reduce-scatter of the q.k partial sums over the lanes
 //     of a token, warp-shuffle maxima, per-warp online softmax;
 //   * per-request lengths come from a device vector (no host synchronisation);
@@ -31,7 +32,11 @@ struct DecodeCfg {
   static constexpr int kEPV = 16 / (int)sizeof(T);   // elements per 16-byte vector
   static constexpr int kLPT = D / kEPV;               // lanes per token
   static constexpr int kTPP = 32 / kLPT;              // tokens per warp pass
-  static constexpr int kWarps = 4;                    // consumer warps
+  // consumer warps: the per-tile work of a warp is a chain of dependent
+  // shuffles and exponentials, so more warps hide more of its latency; with 4
+  // or more query heads per KV head the per-warp reduction buffer of 8 warps
+  // would leave room for only one CTA per SM
+  static constexpr int kWarps = G <= 2 ? 8 : 4;
   static constexpr int kThreads = (kWarps + 1) * 32;  // + 1 producer warp
   static constexpr int kTileBytes = 16384;
   static constexpr int kTile = kTileBytes / kRowBytes;  // tokens per stage
@@ -39,7 +44,7 @@ struct DecodeCfg {
   static constexpr int kNP = kTPW / kTPP;               // passes per tile
   static constexpr int kNV = kNP * G;                   // partial scores per lane
   static constexpr int kLogLPT = kLPT == 1 ? 0 : kLPT == 2 ? 1 : kLPT == 4 ? 2 : kLPT == 8 ? 3 : kLPT == 16 ? 4 : 5;
-  static constexpr int kLogNP = kNP == 8 ? 3 : -1;
+  static constexpr int kLogNP = kNP == 4 ? 2 : kNP == 8 ? 3 : -1;
   // halving steps of the reduce-scatter: stop once a lane holds one full pass (G values)
   static constexpr int kHalve = kLogLPT < kLogNP ? kLogLPT : kLogNP;
   static constexpr int kRV = kNV >> kHalve;            // values kept per lane (multiple of G)
@@ -58,7 +63,7 @@ struct DecodeCfg {
   static constexpr int kSmemBytes = kOffRed + (kRedFloats + kPFloats) * 4 + 16;
   static_assert(kEPV * kLPT == D, "head_dim must be a multiple of the vector width");
   static_assert(kLPT <= 32 && kTPP * kLPT == 32, "lanes per token must divide 32");
-  static_assert(kNP == 8, "tile geometry");
+  static_assert(kLogNP >= 0, "tile geometry");
   static_assert(kRV % G == 0, "each lane must keep whole passes");
   static_assert(kQBytes % 16 == 0 && kEntryBytes % 16 == 0, "queue entries hold 16-byte aligned copies");
 };
@@ -68,7 +73,7 @@ struct DecodeItem {
   int b, kvh, split, t0, ntok, nsplit;
 };
 
-// Consumer-warp barrier (named barrier 1, the 4 consumer warps only): every
+// Consumer-warp barrier (named barrier 1, the consumer warps only): every
 // consumer warp reaches each use exactly once per item, also on the abort
 // path, so the producer warp never takes part and never blocks it.
 template <int kWarps>
@@ -97,7 +102,7 @@ __device__ __forceinline__ bool consumer_any(bool pred) {
 // items, so the copies for the next item are in flight while the consumers
 // finish the current one.
 template <typename T, int D, int G>
-__global__ void __launch_bounds__(DecodeCfg<T, D, G>::kThreads)
+__global__ void __launch_bounds__(DecodeCfg<T, D, G>::kThreads, G <= 2 ? 2 : 1)
     decode_gqa_kernel(const DecodeArgs a) {
   using C = DecodeCfg<T, D, G>;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -268,7 +273,7 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kThreads)
       const bool got = mbar_wait(qfull0 + 8 * slot, (qi / C::kQueue) & 1, &s_abort, a.err);
       const DecodeItem it = *reinterpret_cast<const DecodeItem*>(queue + slot * C::kEntryBytes);
       // every consumer warp leaves at the same item (the named barriers below
-      // need all four): the stop decision is OR-reduced over them
+      // need every one): the stop decision is OR-reduced over them
       if (consumer_any<C::kWarps>(!got || it.ntok < 0 || s_abort != 0)) break;
       float qf[G][C::kEPV];
       float o[G][C::kEPV];
