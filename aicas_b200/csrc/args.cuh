@@ -5,6 +5,41 @@
 
 namespace aicas {
 
+#if defined(__CUDACC__)
+#define AICAS_HD __host__ __device__ __forceinline__
+#else
+#define AICAS_HD inline
+#endif
+
+// Split-KV table of the decode kernel, shared by the host plan (workspace size)
+// and the kernel (each item's token range).  split_floor == 0: every split
+// holds split_tokens tokens.  split_floor > 0: a halving table, split 0 holds
+// split_tokens tokens and split s >= 1 holds split_tokens >> s rounded up to
+// whole tiles, never fewer than split_floor; the splits handed out last are
+// then the short ones, which evens out when the CTAs finish.
+AICAS_HD int decode_split_size(int s, int split_tokens, int split_floor, int tile) {
+  if (split_floor == 0 || s == 0) return split_tokens;
+  const int h = s < 30 ? (split_tokens >> s) : 0;
+  const int r = (h + tile - 1) / tile * tile;
+  return r > split_floor ? r : split_floor;
+}
+AICAS_HD int decode_split_start(int s, int split_tokens, int split_floor, int tile) {
+  if (split_floor == 0) return s * split_tokens;
+  int t = 0;
+  for (int i = 0; i < s; ++i) t += decode_split_size(i, split_tokens, split_floor, tile);
+  return t;
+}
+// number of splits of a cache of len tokens (at least one)
+AICAS_HD int decode_split_count(int len, int split_tokens, int split_floor, int tile) {
+  if (split_floor == 0) return len <= split_tokens ? 1 : (len + split_tokens - 1) / split_tokens;
+  int t = 0, n = 0;
+  do {
+    t += decode_split_size(n, split_tokens, split_floor, tile);
+    ++n;
+  } while (t < len);
+  return n;
+}
+
 struct DecodeArgs {
   const void* q;
   const void* k;
@@ -16,7 +51,8 @@ struct DecodeArgs {
   int64_t q_sb, q_sh, k_sb, k_sh, v_sb, v_sh, o_sb, o_sh;
   int batch, hq, hkv, cap;
   float scale_log2;
-  int split_tokens;
+  int split_tokens;       // tokens of split 0 (of every split when split_floor == 0)
+  int split_floor;        // 0: fixed splits; > 0: halving table (decode_split_size)
   int max_splits;
   float* ws_o;            // [B*Hkv, max_splits, G, D]
   float* ws_lse;          // [B*Hkv, max_splits, G]

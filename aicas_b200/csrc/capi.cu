@@ -2,6 +2,7 @@
 // Nothing here allocates device memory or synchronises the device (except the
 // one-time peer-buffer set-up calls aicas_peer_buffer_alloc/free, and
 // the explicit health query aicas_device_error_flags).
+#include <algorithm>
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
@@ -102,6 +103,7 @@ constexpr int kMaxSplitUnits = (int)(kSchedOffset / sizeof(unsigned int));
 // Split-KV plan shared by aicas_decode_workspace_bytes and aicas_decode_gqa.
 struct DecodePlan {
   int split_tokens;
+  int split_floor;
   int max_splits;
   size_t ws_o_off, ws_lse_off, ws_count_off, ws_bytes;
 };
@@ -109,6 +111,7 @@ struct DecodePlan {
 int plan_decode(const aicas_decode_params* p, DecodePlan* out) {
   const int tile = aicas::decode_tile_for(p->dtype, p->head_dim);
   int split = p->split_tokens;
+  int split_floor = 0;
   if (split < 0 || (split > 0 && split % tile != 0))
     return fail(AICAS_ERR_UNSUPPORTED, "split_tokens=%d must be 0 or a positive multiple of %d",
                 p->split_tokens, tile);
@@ -119,24 +122,41 @@ int plan_decode(const aicas_decode_params* p, DecodePlan* out) {
     // pairs, about one item per resident CTA (one wave, no boundaries); with
     // many pairs of ragged lengths, about five items per CTA so that the
     // dynamic hand-out can even out the lengths.
+    //
+    // In the second case the splits of a cache shrink: split 0 is 1.4x that
+    // size (at most half the capacity), the next ones halve down to a quarter
+    // of it.  Items are handed out split-major, so the long first splits go
+    // first and the short late ones fill in as the CTAs finish, which shortens
+    // the tail of the launch (ragged config-2 lengths: ~8 % less time than
+    // equal splits).
     const int64_t cap = p->kv_capacity > 0 ? p->kv_capacity : 1;
     const int64_t pairs = (int64_t)p->batch * p->num_kv_heads;
     const int64_t resident = (int64_t)sm_count() * 2;
+    const auto round_tiles = [&](int64_t v) {
+      v = (v + tile - 1) / tile * tile;
+      return v < 4 * tile ? (int64_t)4 * tile : v;
+    };
     int64_t s;
     if (2 * pairs <= resident) {
       const int64_t per_pair = resident / pairs;
-      s = (cap + per_pair - 1) / per_pair;
+      s = round_tiles((cap + per_pair - 1) / per_pair);
     } else {
-      s = (cap * pairs + 5 * resident - 1) / (5 * resident);
+      s = round_tiles((cap * pairs + 5 * resident - 1) / (5 * resident));
+      if (s < cap) {  // (else one split per cache: the pairs alone balance the CTAs)
+        const int64_t s0 = std::min(round_tiles(s * 7 / 5), round_tiles(cap / 2));
+        split_floor = (int)round_tiles(s0 / 4);
+        s = s0;
+        if (split_floor >= s) split_floor = 0;  // nothing to halve
+      }
     }
-    s = (s + tile - 1) / tile * tile;
-    if (s < 4 * tile) s = 4 * tile;
     if (s > 16384) s = 16384;
+    if (split_floor > s) split_floor = 0;
     split = (int)s;
   }
   const int cap = p->kv_capacity > 0 ? p->kv_capacity : 1;
   out->split_tokens = split;
-  out->max_splits = (cap + split - 1) / split;
+  out->split_floor = split_floor;
+  out->max_splits = aicas::decode_split_count(cap, split, split_floor, tile);
   const int g = p->num_q_heads / p->num_kv_heads;
   const size_t units = (size_t)p->batch * p->num_kv_heads;
   if (out->max_splits > 1 && units > kMaxSplitUnits)
@@ -361,6 +381,7 @@ int aicas_decode_gqa(const aicas_decode_params* p, void* workspace, size_t works
   a.batch = p->batch; a.hq = p->num_q_heads; a.hkv = p->num_kv_heads; a.cap = p->kv_capacity;
   a.scale_log2 = p->sm_scale * 1.4426950408889634f;
   a.split_tokens = plan.split_tokens;
+  a.split_floor = plan.split_floor;
   a.max_splits = plan.max_splits;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   a.ws_o = plan.ws_bytes ? reinterpret_cast<float*>(ws + plan.ws_o_off) : nullptr;

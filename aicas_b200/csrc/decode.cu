@@ -147,8 +147,8 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kThreads, G <= 2 ? 2 : 1)
     // K/V can be brought into L2 while the kernel before this one finishes
     const int bh = (int)blockIdx.x % (a.batch * a.hkv), split = (int)blockIdx.x / (a.batch * a.hkv);
     const int b = bh / a.hkv, kvh = bh % a.hkv;
-    const int t0 = split * a.split_tokens;
-    const int ntok = min(a.cap, t0 + a.split_tokens) - t0;
+    const int t0 = decode_split_start(split, a.split_tokens, a.split_floor, C::kTile);
+    const int ntok = min(a.cap, t0 + decode_split_size(split, a.split_tokens, a.split_floor, C::kTile)) - t0;
     if (ntok > 0) {
       const uint8_t* gk = static_cast<const uint8_t*>(a.k) +
                           ((int64_t)b * a.k_sb + (int64_t)kvh * a.k_sh + (int64_t)t0 * D) * sizeof(T);
@@ -195,10 +195,11 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kThreads, G <= 2 ? 2 : 1)
           it.kvh = bh % a.hkv;
           int len = a.cap;
           if (a.kv_lens != nullptr) len = min(max(__ldg(a.kv_lens + it.b), 0), a.cap);
-          it.nsplit = max(1, (len + a.split_tokens - 1) / a.split_tokens);
+          it.nsplit = decode_split_count(len, a.split_tokens, a.split_floor, C::kTile);
           if (it.split >= it.nsplit) continue;  // past this request's length
-          it.t0 = it.split * a.split_tokens;
-          it.ntok = max(0, min(len, it.t0 + a.split_tokens) - it.t0);
+          it.t0 = decode_split_start(it.split, a.split_tokens, a.split_floor, C::kTile);
+          it.ntok = max(0, min(len, it.t0 + decode_split_size(it.split, a.split_tokens, a.split_floor, C::kTile)) -
+                               it.t0);
           item = cand;
           break;
         }

@@ -78,6 +78,29 @@ def test_decode_shapes_against_oracle(cuda_device, dtype, head_dim, groups):
         np.testing.assert_allclose(_np(lse[b : b + 1]), ref_lse, rtol=0, atol=1e-3)
 
 
+@pytest.mark.parametrize("dtype,head_dim,groups", [("bf16", 128, 2), ("fp16", 64, 1), ("fp32", 128, 4)])
+def test_auto_split_halving_table_against_oracle(cuda_device, dtype, head_dim, groups):
+    """Many (request, KV head) pairs with the automatic split: the halving split
+    table (for bf16 at head_dim 128: 384, 256, 256, 256 tokens at capacity 1024)
+    with lengths on and around every split boundary, empty and full caches."""
+    torch.manual_seed(21 + head_dim + groups)
+    B, Hkv, L = 24, 8, 1024
+    q = torch.randn(B, Hkv * groups, 1, head_dim).to(DT[dtype])
+    k = torch.randn(B, Hkv, L, head_dim).to(DT[dtype])
+    v = torch.randn(B, Hkv, L, head_dim).to(DT[dtype])
+    lens = [0, 1, 255, 256, 257, 383, 384, 385, 639, 640, 641, 895, 896, 897, 1023, 1024]
+    lens += torch.randint(1, L + 1, (B - len(lens),)).tolist()
+    scale = head_dim ** -0.5
+    ref = oa.decode_ragged(_np(q), _np(k), _np(v), lens, scale, groups)
+    out = ab.gqa_decode_attention(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), sm_scale=scale,
+                                  num_key_value_groups=groups, kv_lens=lens)
+    if dtype == "fp32":
+        np.testing.assert_allclose(_np(out), ref, rtol=0, atol=5e-6)
+    else:
+        bf16_tolerance_check(_np(out), ref)
+    assert nat.device_error_flags() == 0
+
+
 def test_workspace_reuse_across_shapes(cuda_device):
     """One workspace serves calls of different shapes and split sizes in a row:
     the split counters sit at a fixed offset and every call leaves them zeroed."""
