@@ -93,6 +93,56 @@ __device__ __forceinline__ bool consumer_any(bool pred) {
   return r != 0;
 }
 
+// Merges the split partials of one (request, KV head) pair into its output and
+// resets the pair's split counter for the next call; run by the consumer
+// threads of the CTA whose increment of that counter came last.  Up to eight
+// splits' partials are loaded before any is used (one L2 round trip).
+template <typename T, int D, int G, int kThreads>
+__device__ void merge_splits(const DecodeArgs& a, int b, int kvh, int nsplit) {
+  constexpr int kMC = 8;
+  const int bh = b * a.hkv + kvh;
+  for (int idx = threadIdx.x; idx < G * D; idx += kThreads) {
+    const int h = idx / D, d = idx % D;
+    float M = -INFINITY, L = 0.f, O = 0.f;
+    for (int sp0 = 0; sp0 < nsplit; sp0 += kMC) {
+      float ls[kMC], os[kMC];
+#pragma unroll
+      for (int j = 0; j < kMC; ++j) {
+        ls[j] = -INFINITY;
+        os[j] = 0.f;
+        if (sp0 + j < nsplit) {
+          const int64_t base = ((int64_t)bh * a.max_splits + sp0 + j) * G + h;
+          ls[j] = __ldcg(a.ws_lse + base);
+          os[j] = __ldcg(a.ws_o + base * D + d);
+        }
+      }
+      float mc = M;
+#pragma unroll
+      for (int j = 0; j < kMC; ++j) mc = fmaxf(mc, ls[j]);
+      if (mc != -INFINITY) {
+        const float r = exp2f(M - mc);  // 0 while nothing has been accumulated
+        L *= r;
+        O *= r;
+#pragma unroll
+        for (int j = 0; j < kMC; ++j) {
+          const float w = exp2f(ls[j] - mc);
+          L += w;
+          O += w * os[j];
+        }
+        M = mc;
+      }
+    }
+    const float ov = (L > 0.f) ? O / L : 0.f;
+    const float lse = (L > 0.f) ? M + log2f(L) : -INFINITY;
+    const int qh = kvh * G + h;
+    if (a.out != nullptr)
+      static_cast<T*>(a.out)[(int64_t)b * a.o_sb + (int64_t)qh * a.o_sh + d] = Elem<T>::from_float(ov);
+    if (a.partial_o != nullptr) a.partial_o[((int64_t)b * a.hq + qh) * D + d] = ov;
+    if (a.lse != nullptr && d == 0) a.lse[(int64_t)b * a.hq + qh] = lse;
+  }
+  if (threadIdx.x == 0) a.ws_count[bh] = 0u;  // ready for the next call
+}
+
 // Persistent CTAs (as many as fit on the device at once) run through the
 // (request, KV head, split) work items.  With a workspace the items are handed
 // out by an atomic counter (ragged cache lengths make a static split
@@ -113,7 +163,7 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kThreads, G <= 2 ? 2 : 1)
   float* red = reinterpret_cast<float*>(smem + C::kOffRed);  // [warp][G][D+2]
   float* ps = red + C::kRedFloats;                             // [tile token][G]
   __shared__ int s_abort;
-  __shared__ int s_last;
+  __shared__ int s_merge[4];  // [merge?, b, kvh, nsplit] of a finished pair, published by thread 0
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -268,6 +318,17 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kThreads, G <= 2 ? 2 : 1)
     const bool canonical = (gl % C::kDup) == 0;
     float* pw = ps + warp * C::kTPW * G;  // this warp's probabilities [token][G]
     uint32_t g = 0;                       // ring position
+    // thread 0: the split-counter increment of the last split item, whose
+    // result is read one item later so that its round trip overlaps the tiles
+    unsigned int pend_prev = 0;
+    int pend_b = -1, pend_kvh = 0, pend_nsplit = 0;
+    const auto publish_pending = [&]() {
+      s_merge[0] = (pend_b >= 0 && pend_prev == (unsigned int)(pend_nsplit - 1)) ? 1 : 0;
+      s_merge[1] = pend_b;
+      s_merge[2] = pend_kvh;
+      s_merge[3] = pend_nsplit;
+      pend_b = -1;
+    };
     for (uint32_t qi = 0;; ++qi) {
       // ---- next item from the queue (every consumer warp takes every item)
       const uint32_t slot = qi % C::kQueue;
@@ -417,6 +478,9 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kThreads, G <= 2 ? 2 : 1)
           rw[D + 1] = l[h];
         }
       }
+      // the previous split's counter increment was issued one item ago: by now
+      // its result is back, and it says whether this CTA merges that pair
+      if (threadIdx.x == 0) publish_pending();
       consumer_sync<C::kWarps>();
 
       // ---- merge the consumer warps: result for (h, d) of this split
@@ -450,47 +514,25 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kThreads, G <= 2 ? 2 : 1)
           if (d == 0) a.ws_lse[((int64_t)bh * a.max_splits + it.split) * G + h] = lse;
         }
       }
-      if (!single) {
-        // ---- split-KV: the last split of this (request, KV head) to finish merges all of them.
-        // The consumer barrier orders this CTA's partial writes before thread
-        // 0's acquire-release increment at GPU scope (cumulative), which in
-        // turn orders the other splits' partials before the merge reads them.
-        consumer_sync<C::kWarps>();
-        if (threadIdx.x == 0) {
-          unsigned int prev;
-          asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(a.ws_count + bh) : "memory");
-          s_last = (prev == (unsigned int)(it.nsplit - 1));
-        }
-        consumer_sync<C::kWarps>();
-        if (s_last) {
-          for (int idx = threadIdx.x; idx < G * D; idx += C::kWarps * 32) {
-            const int h = idx / D, d = idx % D;
-            float M = -INFINITY;
-            for (int sp = 0; sp < it.nsplit; ++sp)
-              M = fmaxf(M, __ldcg(a.ws_lse + ((int64_t)bh * a.max_splits + sp) * G + h));
-            float L = 0.f, O = 0.f;
-            if (M != -INFINITY) {
-              for (int sp = 0; sp < it.nsplit; ++sp) {
-                const int64_t base = ((int64_t)bh * a.max_splits + sp) * G + h;
-                const float w = exp2f(__ldcg(a.ws_lse + base) - M);
-                L += w;
-                O += w * __ldcg(a.ws_o + base * D + d);
-              }
-            }
-            const float ov = (L > 0.f) ? O / L : 0.f;
-            const float lse = (L > 0.f) ? M + log2f(L) : -INFINITY;
-            const int qh = it.kvh * G + h;
-            if (a.out != nullptr)
-              static_cast<T*>(a.out)[(int64_t)it.b * a.o_sb + (int64_t)qh * a.o_sh + d] = Elem<T>::from_float(ov);
-            if (a.partial_o != nullptr) a.partial_o[((int64_t)it.b * a.hq + qh) * D + d] = ov;
-            if (a.lse != nullptr && d == 0) a.lse[(int64_t)it.b * a.hq + qh] = lse;
-          }
-          if (threadIdx.x == 0) a.ws_count[bh] = 0u;  // ready for the next call
-        }
-      }
-      // the reductions buffer and s_last are reused by the next item
+      if (s_merge[0]) merge_splits<T, D, G, C::kWarps * 32>(a, s_merge[1], s_merge[2], s_merge[3]);
+      // the reductions buffer and s_merge are reused by the next item; for a
+      // split this barrier also orders the CTA's partial writes before thread
+      // 0's acquire-release increment of the pair's split counter at GPU scope
+      // (cumulative), which in turn orders every split's partials before the
+      // merge that the last increment triggers
       consumer_sync<C::kWarps>();
+      if (!single && threadIdx.x == 0) {
+        // issued now, read at the next item's end (or after the last item)
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(pend_prev) : "l"(a.ws_count + bh) : "memory");
+        pend_b = it.b;
+        pend_kvh = it.kvh;
+        pend_nsplit = it.nsplit;
+      }
     }
+    // ---- the last item's increment: merge its pair if that came last
+    if (threadIdx.x == 0) publish_pending();
+    consumer_sync<C::kWarps>();
+    if (s_merge[0] && s_abort == 0) merge_splits<T, D, G, C::kWarps * 32>(a, s_merge[1], s_merge[2], s_merge[3]);
   }
 
   // ---- scheduling counters back to zero for the next call: the last CTA out resets them
