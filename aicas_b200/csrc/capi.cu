@@ -124,7 +124,7 @@ int plan_decode(const aicas_decode_params* p, DecodePlan* out) {
     // dynamic hand-out can even out the lengths.
     //
     // In the second case the splits of a cache shrink: split 0 is 1.4x that
-    // size (at most half the capacity), the next ones halve down to a quarter
+    // size (at most half the capacity), the next ones halve down to an eighth
     // of it.  Items are handed out split-major, so the long first splits go
     // first and the short late ones fill in as the CTAs finish, which shortens
     // the tail of the launch (ragged config-2 lengths: ~8 % less time than
@@ -144,7 +144,7 @@ int plan_decode(const aicas_decode_params* p, DecodePlan* out) {
       s = round_tiles((cap * pairs + 5 * resident - 1) / (5 * resident));
       if (s < cap) {  // (else one split per cache: the pairs alone balance the CTAs)
         const int64_t s0 = std::min(round_tiles(s * 7 / 5), round_tiles(cap / 2));
-        split_floor = (int)round_tiles(s0 / 4);
+        split_floor = (int)round_tiles(s0 / 8);
         s = s0;
         if (split_floor >= s) split_floor = 0;  // nothing to halve
       }

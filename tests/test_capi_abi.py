@@ -125,7 +125,7 @@ def test_decode_workspace_is_required_for_split_kv(native_lib):
 def test_decode_auto_split_table(native_lib):
     """Automatic split (148 SMs, 2 CTAs each).  Ragged batch of 512 (request,
     KV head) pairs at capacity 4096: equal splits would hold 1472 tokens; the
-    halving table holds 2048, 1024, 512, 512 -> 4 partial slots per pair.
+    halving table holds 2048, 1024, 512, 256, 256 -> 5 partial slots per pair.
     32 pairs: about one item per resident CTA (9 per pair -> 512 tokens,
     8 slots).  2048 pairs at capacity 2048: one split each, no workspace."""
 
@@ -136,7 +136,7 @@ def test_decode_auto_split_table(native_lib):
         e = up((1 << 20) + units * splits * 2 * 128 * 4)
         return up(e + units * splits * 2 * 4)
 
-    assert native_lib.aicas_decode_workspace_bytes(ctypes.byref(_decode_params())) == ws(512, 4)
+    assert native_lib.aicas_decode_workspace_bytes(ctypes.byref(_decode_params())) == ws(512, 5)
     assert native_lib.aicas_decode_workspace_bytes(ctypes.byref(_decode_params(batch=4))) == ws(32, 8)
     p = _decode_params(batch=256, kv_capacity=2048)
     assert native_lib.aicas_decode_workspace_bytes(ctypes.byref(p)) == 0
