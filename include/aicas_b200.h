@@ -111,7 +111,9 @@ typedef struct aicas_decode_params {
   int32_t kv_capacity;     /* L: allocated cache length, upper bound of kv_lens */
   int32_t dtype;           /* AICAS_DTYPE_* of q, k, v, out */
   float sm_scale;
-  int32_t split_tokens;    /* tokens per split-KV work unit; 0 = choose automatically */
+  int32_t split_tokens;    /* tokens per split-KV work unit; 0 = choose automatically (for
+                              many (request, KV head) pairs a halving table: the first split
+                              of each cache the longest, later ones down to 1/8 of it) */
 } aicas_decode_params;
 
 /* Bytes of device workspace aicas_decode_gqa needs for these parameters (0 when
