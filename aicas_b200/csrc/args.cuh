@@ -29,14 +29,19 @@ AICAS_HD int decode_split_start(int s, int split_tokens, int split_floor, int ti
   for (int i = 0; i < s; ++i) t += decode_split_size(i, split_tokens, split_floor, tile);
   return t;
 }
-// number of splits of a cache of len tokens (at least one)
-AICAS_HD int decode_split_count(int len, int split_tokens, int split_floor, int tile) {
+// Number of splits of a cache of len tokens (at least one).  In the halving
+// table a last split that would hold fewer than split_floor tokens is folded
+// into the split before it (absorb), which then runs to len: a cache just past
+// a split boundary costs no extra item.  Without absorb: the table's own count,
+// an upper bound for every len up to this one (the workspace's slot count).
+AICAS_HD int decode_split_count(int len, int split_tokens, int split_floor, int tile, bool absorb = true) {
   if (split_floor == 0) return len <= split_tokens ? 1 : (len + split_tokens - 1) / split_tokens;
   int t = 0, n = 0;
   do {
     t += decode_split_size(n, split_tokens, split_floor, tile);
     ++n;
   } while (t < len);
+  if (absorb && n > 1 && len - (t - decode_split_size(n - 1, split_tokens, split_floor, tile)) < split_floor) --n;
   return n;
 }
 

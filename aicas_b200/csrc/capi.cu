@@ -108,7 +108,9 @@ struct DecodePlan {
   size_t ws_o_off, ws_lse_off, ws_count_off, ws_bytes;
 };
 
-int plan_decode(const aicas_decode_params* p, DecodePlan* out) {
+// compact: with many pairs, take whole caches as items whenever the pairs alone
+// balance the CTAs (no workspace then), for callers whose scratch is fixed.
+int plan_decode(const aicas_decode_params* p, DecodePlan* out, bool compact = false) {
   const int tile = aicas::decode_tile_for(p->dtype, p->head_dim);
   int split = p->split_tokens;
   int split_floor = 0;
@@ -142,7 +144,7 @@ int plan_decode(const aicas_decode_params* p, DecodePlan* out) {
       s = round_tiles((cap + per_pair - 1) / per_pair);
     } else {
       s = round_tiles((cap * pairs + 5 * resident - 1) / (5 * resident));
-      if (s < cap) {  // (else one split per cache: the pairs alone balance the CTAs)
+      if (s < cap || !compact) {
         const int64_t s0 = std::min(round_tiles(s * 7 / 5), round_tiles(cap / 2));
         split_floor = (int)round_tiles(s0 / 8);
         s = s0;
@@ -156,7 +158,7 @@ int plan_decode(const aicas_decode_params* p, DecodePlan* out) {
   const int cap = p->kv_capacity > 0 ? p->kv_capacity : 1;
   out->split_tokens = split;
   out->split_floor = split_floor;
-  out->max_splits = aicas::decode_split_count(cap, split, split_floor, tile);
+  out->max_splits = aicas::decode_split_count(cap, split, split_floor, tile, /*absorb=*/false);
   const int g = p->num_q_heads / p->num_kv_heads;
   const size_t units = (size_t)p->batch * p->num_kv_heads;
   if (out->max_splits > 1 && units > kMaxSplitUnits)
@@ -360,12 +362,9 @@ size_t aicas_decode_workspace_bytes(const aicas_decode_params* p) {
   return plan.ws_bytes;
 }
 
-int aicas_decode_gqa(const aicas_decode_params* p, void* workspace, size_t workspace_bytes, void* stream) {
-  int rc = check_decode(p);
-  if (rc != AICAS_OK) return rc;
-  DecodePlan plan;
-  rc = plan_decode(p, &plan);
-  if (rc != AICAS_OK) return rc;
+// Launches the decode of a checked call with its plan.
+int run_decode(const aicas_decode_params* p, const DecodePlan& plan, void* workspace, size_t workspace_bytes,
+               void* stream) {
   if (plan.ws_bytes > 0 && (workspace == nullptr || workspace_bytes < plan.ws_bytes))
     return fail(AICAS_ERR_WORKSPACE, "decode needs %zu bytes of zero-initialised workspace (got %zu)", plan.ws_bytes,
                 workspace_bytes);
@@ -395,12 +394,27 @@ int aicas_decode_gqa(const aicas_decode_params* p, void* workspace, size_t works
   return AICAS_OK;
 }
 
+int aicas_decode_gqa(const aicas_decode_params* p, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_decode(p);
+  if (rc != AICAS_OK) return rc;
+  DecodePlan plan;
+  rc = plan_decode(p, &plan);
+  if (rc != AICAS_OK) return rc;
+  return run_decode(p, plan, workspace, workspace_bytes, stream);
+}
+
 int aicas_decode_gqa_noalloc(const aicas_decode_params* p, void* stream) {
   int rc = check_decode(p);
   if (rc != AICAS_OK) return rc;
   DecodePlan plan;
   rc = plan_decode(p, &plan);
   if (rc != AICAS_OK) return rc;
+  if (plan.ws_bytes > kNoAllocScratchBytes && p->split_tokens == 0) {
+    // the automatic split table needs more slots than the static scratch has:
+    // whole caches as items where the pairs balance the CTAs on their own
+    rc = plan_decode(p, &plan, /*compact=*/true);
+    if (rc != AICAS_OK) return rc;
+  }
   if (plan.ws_bytes > kNoAllocScratchBytes)
     return fail(AICAS_ERR_UNSUPPORTED,
                 "aicas_decode_gqa_noalloc: this call needs %zu bytes of split-KV scratch but the library's static "
@@ -420,7 +434,7 @@ int aicas_decode_gqa_noalloc(const aicas_decode_params* p, void* stream) {
       e = cudaMemsetAsync(static_cast<uint8_t*>(scratch) + kSchedOffset, 0, 64, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "aicas_decode_gqa_noalloc: clearing the split counters");
   }
-  return aicas_decode_gqa(p, scratch, scratch != nullptr ? kNoAllocScratchBytes : 0, stream);
+  return run_decode(p, plan, scratch, scratch != nullptr ? kNoAllocScratchBytes : 0, stream);
 }
 
 int aicas_merge_partials(const aicas_merge_params* p, void* stream) {

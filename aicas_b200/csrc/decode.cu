@@ -248,8 +248,11 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kThreads, G <= 2 ? 2 : 1)
           it.nsplit = decode_split_count(len, a.split_tokens, a.split_floor, C::kTile);
           if (it.split >= it.nsplit) continue;  // past this request's length
           it.t0 = decode_split_start(it.split, a.split_tokens, a.split_floor, C::kTile);
-          it.ntok = max(0, min(len, it.t0 + decode_split_size(it.split, a.split_tokens, a.split_floor, C::kTile)) -
-                               it.t0);
+          // the last split runs to the end of the cache (it may have absorbed a short remainder)
+          const int t1 = it.split == it.nsplit - 1
+                             ? len
+                             : it.t0 + decode_split_size(it.split, a.split_tokens, a.split_floor, C::kTile);
+          it.ntok = max(0, t1 - it.t0);
           item = cand;
           break;
         }

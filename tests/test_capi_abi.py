@@ -127,7 +127,7 @@ def test_decode_auto_split_table(native_lib):
     KV head) pairs at capacity 4096: equal splits would hold 1472 tokens; the
     halving table holds 2048, 1024, 512, 256, 256 -> 5 partial slots per pair.
     32 pairs: about one item per resident CTA (9 per pair -> 512 tokens,
-    8 slots).  2048 pairs at capacity 2048: one split each, no workspace."""
+    8 slots).  2048 pairs at capacity 2048: 1024, 512, 256, 256 -> 4 slots."""
 
     def up(x):
         return (x + 255) // 256 * 256
@@ -139,7 +139,7 @@ def test_decode_auto_split_table(native_lib):
     assert native_lib.aicas_decode_workspace_bytes(ctypes.byref(_decode_params())) == ws(512, 5)
     assert native_lib.aicas_decode_workspace_bytes(ctypes.byref(_decode_params(batch=4))) == ws(32, 8)
     p = _decode_params(batch=256, kv_capacity=2048)
-    assert native_lib.aicas_decode_workspace_bytes(ctypes.byref(p)) == 0
+    assert native_lib.aicas_decode_workspace_bytes(ctypes.byref(p)) == ws(2048, 4)
 
 
 def test_decode_workspace_size_formula(native_lib):

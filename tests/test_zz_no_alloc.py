@@ -88,3 +88,31 @@ def test_noalloc_rejects_requests_beyond_its_static_scratch(cuda_device, native_
     rc = native_lib.aicas_decode_gqa_noalloc(ctypes.byref(p), torch.cuda.current_stream(cuda_device).cuda_stream)
     assert rc == nat.ERR_UNSUPPORTED
     assert "static scratch" in nat.last_error()
+
+
+def test_noalloc_large_batch_takes_whole_caches(cuda_device, native_lib):
+    """256 requests at capacity 2048 with the automatic split: the split table
+    would need more partial slots than the static scratch holds, so the entry
+    point takes whole caches as items (the 2048 pairs balance the CTAs on their
+    own) and needs no scratch; the workspace entry point keeps the table."""
+    stream = torch.cuda.current_stream(cuda_device).cuda_stream
+    batch, hkv, L = 256, 8, 2048
+    g = torch.Generator(device=cuda_device).manual_seed(5)
+    q = torch.randn(batch, 2 * hkv, 1, 128, generator=g, device=cuda_device).to(torch.bfloat16)
+    k = torch.randn(batch, hkv, L, 128, generator=g, device=cuda_device).to(torch.bfloat16)
+    v = torch.randn(batch, hkv, L, 128, generator=g, device=cuda_device).to(torch.bfloat16)
+    lens = torch.randint(1, L + 1, (batch,), generator=g, device=cuda_device, dtype=torch.int32)
+    out_ws = torch.empty_like(q)
+    p_ws = _params(q, k, v, out_ws, lens, 0)
+    need = native_lib.aicas_decode_workspace_bytes(ctypes.byref(p_ws))
+    assert need > 8 << 20  # more than the static scratch
+    ws = torch.zeros(need, dtype=torch.uint8, device=cuda_device)
+    assert native_lib.aicas_decode_gqa(ctypes.byref(p_ws), ws.data_ptr(), need, stream) == nat.OK, nat.last_error()
+    out_na = torch.empty_like(q)
+    p_na = _params(q, k, v, out_na, lens, 0)
+    assert native_lib.aicas_decode_gqa_noalloc(ctypes.byref(p_na), stream) == nat.OK, nat.last_error()
+    torch.cuda.synchronize(cuda_device)
+    ref = oa.decode_ragged(_np(q), _np(k), _np(v), lens.tolist(), q.shape[3] ** -0.5, 2)
+    bf16_tolerance_check(_np(out_na), ref)
+    bf16_tolerance_check(_np(out_ws), ref)
+    assert nat.device_error_flags() == 0
