@@ -38,7 +38,10 @@ _WORKSPACES: dict[tuple[int, int], torch.Tensor] = {}
 
 
 def _stream_handle(device: torch.device) -> int:
-    return torch.cuda.current_stream(device).cuda_stream
+    # an integer index: torch resolves a torch.device argument through a much
+    # slower path, which showed up as a large share of a decode step's host time
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    return torch.cuda.current_stream(idx).cuda_stream
 
 
 def _ptr(t: torch.Tensor | None) -> int | None:
