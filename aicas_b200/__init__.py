@@ -20,10 +20,15 @@ from .ops import (
 )
 from .patch import install_qwen3vl_triton_attention
 
-# Compatibility name: in the reference it says whether Triton imported
-# (dense_flash_attention.py:7-15); here it says whether the native library loads.
-TRITON_AVAILABLE = _native.available()
-NATIVE_AVAILABLE = TRITON_AVAILABLE
+
+def __getattr__(name: str):
+    """``TRITON_AVAILABLE`` / ``NATIVE_AVAILABLE``: in the reference the first
+    says whether Triton imported (dense_flash_attention.py:7-15); here both say
+    whether the native library loads.  They are computed on first use, so that
+    importing the package (for its seeded workloads, say) maps no library."""
+    if name in ("TRITON_AVAILABLE", "NATIVE_AVAILABLE"):
+        return _native.available()
+    raise AttributeError(f"module {__name__!r} has no attribute {name!r}")
 
 __all__ = [
     "NATIVE_AVAILABLE",

@@ -60,6 +60,7 @@ class DecodeParams(ctypes.Structure):
         ("o_stride_b", _i64), ("o_stride_h", _i64),
         ("batch", _i32), ("num_q_heads", _i32), ("num_kv_heads", _i32), ("head_dim", _i32),
         ("kv_capacity", _i32), ("dtype", _i32), ("sm_scale", _f32), ("split_tokens", _i32),
+        ("kv_starts", _vp),
     ]
 
 
@@ -81,7 +82,7 @@ class ExchangeParams(ctypes.Structure):
         ("peers", _vp * MAX_EXCHANGE_RANKS), ("partial_o", _vp), ("partial_lse", _vp), ("out", _vp), ("lse", _vp),
         ("o_stride_b", _i64), ("o_stride_h", _i64),
         ("world", _i32), ("rank", _i32), ("batch", _i32), ("num_heads", _i32), ("head_dim", _i32),
-        ("dtype", _i32),
+        ("dtype", _i32), ("wait_budget_ns", ctypes.c_uint64),
     ]
 
 
@@ -94,7 +95,7 @@ class FmhaParams(ctypes.Structure):
         ("o_stride_b", _i64), ("o_stride_h", _i64), ("o_stride_s", _i64),
         ("batch", _i32), ("num_q_heads", _i32), ("num_kv_heads", _i32), ("seq_len_q", _i32),
         ("seq_len_kv", _i32), ("head_dim", _i32), ("dtype", _i32), ("sm_scale", _f32),
-        ("cu_seqlens_q", _vp), ("cu_seqlens_k", _vp), ("num_seqs", _i32),
+        ("cu_seqlens_q", _vp), ("cu_seqlens_k", _vp), ("num_seqs", _i32), ("kv_starts", _vp),
     ]
 
 
@@ -230,7 +231,24 @@ def capabilities() -> int:
     return int(lib().aicas_capabilities())
 
 
+# called when the device error word is found non-zero: the workspaces whose
+# counters a kernel cut short by a failed wait may have left non-zero are
+# zero-filled again (the header's rule for reusing them)
+_ERROR_HOOKS: list = []
+
+
+def add_device_error_hook(fn) -> None:
+    if fn not in _ERROR_HOOKS:
+        _ERROR_HOOKS.append(fn)
+
+
 def device_error_flags(clear: bool = False) -> int:
+    """AICAS_DEVERR_* bits of the current device (synchronises it).  When any bit
+    is set, the operators' split-KV and decode-product workspaces are
+    zero-filled again before this returns."""
     flags = ctypes.c_uint32(0)
     check(lib().aicas_device_error_flags(ctypes.byref(flags), int(clear)), "aicas_device_error_flags")
+    if flags.value:
+        for fn in _ERROR_HOOKS:
+            fn()
     return int(flags.value)

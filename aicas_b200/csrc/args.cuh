@@ -53,6 +53,7 @@ struct DecodeArgs {
   float* lse;
   float* partial_o;
   const int32_t* kv_lens;
+  const int32_t* kv_starts;  // optional: first valid slot per request (left padding)
   int64_t q_sb, q_sh, k_sb, k_sh, v_sb, v_sh, o_sb, o_sh;
   int batch, hq, hkv, cap;
   float scale_log2;
@@ -110,6 +111,7 @@ struct ExchangeArgs {
   int64_t o_sb, o_sh;
   int world, rank, batch, heads, hd;
   int slot_floats;
+  unsigned long long wait_budget_ns;  // give up on the peers after this long
   unsigned int* err;               // device error word
 };
 

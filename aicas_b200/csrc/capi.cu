@@ -7,6 +7,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 
 #include "common.cuh"
 #include "fmha.cuh"
@@ -78,17 +79,71 @@ int sm_count() {
   return cached[dev];
 }
 
-// Device address of g_device_error for the current device (cached per device).
-unsigned int* device_error_word() {
-  static unsigned int* cached[64] = {nullptr};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  if (cached[dev] == nullptr) {
+// The calling thread's current CUDA context (the driver's cuCtxGetCurrent,
+// fetched through the runtime so the library links no driver library); NULL
+// before the runtime has made one current.
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+CUcontext current_context() {
+  static const CtxGetCurrentFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<CtxGetCurrentFn>(p);
+  }();
+  CUcontext c = nullptr;
+  if (fn == nullptr || fn(&c) != CUDA_SUCCESS) return nullptr;
+  return c;
+}
+
+// Device addresses of a __device__ array, one per CUDA context: a module's
+// globals live at a different address in every context (a host may create
+// its own contexts next to the runtime's primary one), so the address is
+// looked up once per context, with that context current.
+class SymbolAddresses {
+ public:
+  explicit SymbolAddresses(const void* symbol) : symbol_(symbol) {}
+  cudaError_t get(void** out) {
+    CUcontext ctx = current_context();
+    {
+      std::lock_guard<std::mutex> lock(mu_);
+      for (int i = 0; i < n_ && ctx != nullptr; ++i)
+        if (entries_[i].ctx == ctx) {
+          *out = entries_[i].ptr;
+          return cudaSuccess;
+        }
+    }
     void* ptr = nullptr;
-    if (cudaGetSymbolAddress(&ptr, g_device_error) != cudaSuccess) return nullptr;
-    cached[dev] = static_cast<unsigned int*>(ptr);
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, symbol_);
+    if (e != cudaSuccess) return e;
+    if (ptr == nullptr) return cudaErrorInvalidSymbol;
+    if (ctx == nullptr) ctx = current_context();  // the lookup above made the primary context current
+    {
+      std::lock_guard<std::mutex> lock(mu_);
+      if (ctx != nullptr && n_ < kMax) entries_[n_++] = {ctx, ptr};
+    }
+    *out = ptr;
+    return cudaSuccess;
   }
-  return cached[dev];
+
+ private:
+  static constexpr int kMax = 256;
+  struct Entry {
+    CUcontext ctx;
+    void* ptr;
+  };
+  const void* symbol_;
+  std::mutex mu_;
+  Entry entries_[kMax] = {};
+  int n_ = 0;
+};
+
+// Device address of g_device_error in the current context.
+unsigned int* device_error_word() {
+  static SymbolAddresses addresses(reinterpret_cast<const void*>(&g_device_error));
+  void* ptr = nullptr;
+  return addresses.get(&ptr) == cudaSuccess ? static_cast<unsigned int*>(ptr) : nullptr;
 }
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -161,6 +216,10 @@ int plan_decode(const aicas_decode_params* p, DecodePlan* out, bool compact = fa
   out->max_splits = aicas::decode_split_count(cap, split, split_floor, tile, /*absorb=*/false);
   const int g = p->num_q_heads / p->num_kv_heads;
   const size_t units = (size_t)p->batch * p->num_kv_heads;
+  // the kernel numbers work items (request, KV head, split) with 32-bit ints
+  if ((int64_t)units * out->max_splits > (int64_t)INT32_MAX)
+    return fail(AICAS_ERR_UNSUPPORTED, "%zu (request, KV head) pairs x %d splits exceed the 2^31 work items of one launch",
+                units, out->max_splits);
   if (out->max_splits > 1 && units > kMaxSplitUnits)
     return fail(AICAS_ERR_UNSUPPORTED, "split-KV decode supports at most %d (request, KV head) pairs (got %zu)",
                 kMaxSplitUnits, units);
@@ -234,6 +293,7 @@ int check_fmha(const aicas_fmha_params* p, bool varlen) {
     if (p->num_q_heads != p->num_kv_heads) return fail(AICAS_ERR_UNSUPPORTED, "varlen attention needs Hq == Hkv");
     if (p->cu_seqlens_q == nullptr || p->cu_seqlens_k == nullptr || p->num_seqs < 0)
       return fail(AICAS_ERR_INVALID, "cu_seqlens_q/k must be set");
+    if (p->kv_starts != nullptr) return fail(AICAS_ERR_UNSUPPORTED, "kv_starts applies to causal prefill only");
   } else {
     if (p->seq_len_q != p->seq_len_kv)
       return fail(AICAS_ERR_UNSUPPORTED, "causal prefill needs q_len == kv_len (%d vs %d)", p->seq_len_q, p->seq_len_kv);
@@ -252,24 +312,14 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 
 namespace {
 
-// Device address of g_noalloc_scratch on the current device.  In host code the
+// Device address of g_noalloc_scratch in the current context.  In host code the
 // array's name only stands in for the symbol: the address must be looked up
-// (once per device, with that device current) before a kernel may use it.
+// (once per context, with that context current) before a kernel may use it.
 int noalloc_scratch(void** out) {
-  static std::atomic<void*> cached[64];
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return cuda_fail(e, "aicas_decode_gqa_noalloc: cudaGetDevice");
-  if (dev < 0 || dev >= 64) return fail(AICAS_ERR_UNSUPPORTED, "aicas_decode_gqa_noalloc: device %d out of range", dev);
-  void* ptr = cached[dev].load();
-  if (ptr == nullptr) {
-    e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
-    if (e != cudaSuccess || ptr == nullptr)
-      return cuda_fail(e != cudaSuccess ? e : cudaErrorInvalidSymbol,
-                       "aicas_decode_gqa_noalloc: cudaGetSymbolAddress of the static scratch");
-    cached[dev].store(ptr);
-  }
-  *out = ptr;
+  static SymbolAddresses addresses(reinterpret_cast<const void*>(&g_noalloc_scratch));
+  const cudaError_t e = addresses.get(out);
+  if (e != cudaSuccess)
+    return cuda_fail(e, "aicas_decode_gqa_noalloc: cudaGetSymbolAddress of the static scratch");
   return AICAS_OK;
 }
 
@@ -332,7 +382,7 @@ int check_linear(const aicas_linear_params* p) {
 
 extern "C" {
 
-const char* aicas_version(void) { return "aicas_b200 0.1.0 sm_100a abi 1"; }
+const char* aicas_version(void) { return "aicas_b200 0.2.0 sm_100a abi 2"; }
 
 uint32_t aicas_capabilities(void) {
   return AICAS_CAP_DECODE | AICAS_CAP_MERGE | AICAS_CAP_ROPE_APPEND | AICAS_CAP_PEER_EXCHANGE |
@@ -373,6 +423,7 @@ int run_decode(const aicas_decode_params* p, const DecodePlan& plan, void* works
   aicas::DecodeArgs a;
   a.q = p->q; a.k = p->k; a.v = p->v; a.out = p->out; a.lse = p->lse; a.partial_o = p->partial_o;
   a.kv_lens = p->kv_lens;
+  a.kv_starts = p->kv_starts;
   a.q_sb = p->q_stride_b; a.q_sh = p->q_stride_h;
   a.k_sb = p->k_stride_b; a.k_sh = p->k_stride_h;
   a.v_sb = p->v_stride_b; a.v_sh = p->v_stride_h;
@@ -529,6 +580,7 @@ int aicas_exchange_merge(const aicas_exchange_params* p, void* stream) {
   a.heads = p->num_heads;
   a.hd = p->head_dim;
   a.slot_floats = (int)aicas::exchange_slot_floats(p->batch, p->num_heads, p->head_dim);
+  a.wait_budget_ns = p->wait_budget_ns != 0 ? p->wait_budget_ns : aicas::kWaitBudgetNs;
   a.err = device_error_word();
   const cudaError_t e = aicas::launch_exchange_merge(p->dtype, a, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "exchange merge launch");

@@ -245,9 +245,11 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kThreads, G <= 2 ? 2 : 1)
           it.kvh = bh % a.hkv;
           int len = a.cap;
           if (a.kv_lens != nullptr) len = min(max(__ldg(a.kv_lens + it.b), 0), a.cap);
-          it.nsplit = decode_split_count(len, a.split_tokens, a.split_floor, C::kTile);
+          // valid slots [start, len): a left-padded request starts past its padding
+          const int start = a.kv_starts != nullptr ? min(max(__ldg(a.kv_starts + it.b), 0), len) : 0;
+          it.nsplit = decode_split_count(len - start, a.split_tokens, a.split_floor, C::kTile);
           if (it.split >= it.nsplit) continue;  // past this request's length
-          it.t0 = decode_split_start(it.split, a.split_tokens, a.split_floor, C::kTile);
+          it.t0 = start + decode_split_start(it.split, a.split_tokens, a.split_floor, C::kTile);
           // the last split runs to the end of the cache (it may have absorbed a short remainder)
           const int t1 = it.split == it.nsplit - 1
                              ? len

@@ -6,14 +6,18 @@
 //   [0, 256)     uint64 flags[32]: flags[src] = last epoch rank src published here
 //   [256, 264)   uint64 epoch: calls completed by the owner (advanced on the device,
 //                so a captured graph replays correctly)
+//   [264, 268)   uint32 CTAs of the current call that have finished
 //   [512, ...)   fp32 slots[2][world][slot_floats]: the (out, lse) partial of each
 //                source rank, double-buffered by epoch parity
-// One CTA per call: it writes the local partial into slot [parity][rank] of
-// every rank's buffer (plain stores over NVLink), fences at system scope and
-// publishes the epoch with a release store into each peer's flags[rank];
-// then it waits (bounded) until every rank's flag in its own buffer has
-// reached the epoch, and merges the partials exactly as the single-device
-// merge does: o = sum_r 2^(lse_r - M) o_r / sum_r 2^(lse_r - M).
+// One CTA per destination rank: CTA p writes the local partial into slot
+// [parity][rank] of rank p's buffer (plain stores over NVLink, every
+// destination in parallel), fences at system scope and publishes the epoch
+// with a release store into rank p's flags[rank].  Every CTA then waits
+// (bounded) until all ranks' flags in its own buffer have reached the epoch
+// and merges its share of the (request, head) rows exactly as the
+// single-device merge does: o = sum_r 2^(lse_r - M) o_r / sum_r 2^(lse_r - M).
+// The last CTA to finish advances the epoch, so every CTA of a call reads the
+// same epoch whatever order they start in.
 //
 // Slot reuse is safe with two parities: a rank overwrites parity p again only
 // in call e + 2, after its call e + 1 has seen every peer's flag for e + 1,
@@ -25,7 +29,7 @@
 namespace aicas {
 namespace {
 
-constexpr int kExchangeThreads = 512;
+constexpr int kExchangeThreads = 256;
 constexpr size_t kSlotOffset = 512;
 
 __device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
@@ -40,34 +44,38 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long
 template <typename T>
 __global__ void __launch_bounds__(kExchangeThreads) exchange_merge_kernel(const ExchangeArgs a) {
   __shared__ int timed_out;
+  // launched with programmatic dependent launch: the partials come from the
+  // kernel before this one, and so (through it) does the previous call's epoch
+  grid_dependency_wait();
   uint8_t* own = static_cast<uint8_t*>(a.peers[a.rank]);
   unsigned long long* flags = reinterpret_cast<unsigned long long*>(own);
   unsigned long long* epoch_word = reinterpret_cast<unsigned long long*>(own + 256);
-  const unsigned long long e = *epoch_word + 1;
+  unsigned int* done_word = reinterpret_cast<unsigned int*>(own + 264);
+  const unsigned long long e = *reinterpret_cast<volatile unsigned long long*>(epoch_word) + 1;
   const int par = (int)(e & 1);
   const int nbh = a.batch * a.heads;
   const int n_o = nbh * a.hd;
+  const int dst = blockIdx.x;  // destination rank of this CTA's push
   if (threadIdx.x == 0) timed_out = 0;
 
-  // 1. publish the local partial into every rank's buffer (own included)
-  for (int p = 0; p < a.world; ++p) {
-    float* dst = reinterpret_cast<float*>(static_cast<uint8_t*>(a.peers[p]) + kSlotOffset) +
-                 ((size_t)par * a.world + a.rank) * a.slot_floats;
+  // 1. publish the local partial into rank dst's buffer (own buffer for dst == rank)
+  {
+    float* slot = reinterpret_cast<float*>(static_cast<uint8_t*>(a.peers[dst]) + kSlotOffset) +
+                  ((size_t)par * a.world + a.rank) * a.slot_floats;
     const float4* src4 = reinterpret_cast<const float4*>(a.po);
-    float4* dst4 = reinterpret_cast<float4*>(dst);
-    for (int i = threadIdx.x; i < n_o / 4; i += blockDim.x) dst4[i] = src4[i];
-    for (int i = threadIdx.x; i < nbh; i += blockDim.x) dst[n_o + i] = a.plse[i];
+    float4* dst4 = reinterpret_cast<float4*>(slot);
+    for (int i = threadIdx.x; i < n_o / 4; i += blockDim.x) dst4[i] = __ldg(src4 + i);
+    for (int i = threadIdx.x; i < nbh; i += blockDim.x) slot[n_o + i] = __ldg(a.plse + i);
   }
   __threadfence_system();
   __syncthreads();
-  if (threadIdx.x < a.world)
-    st_release_sys(reinterpret_cast<unsigned long long*>(a.peers[threadIdx.x]) + a.rank, e);
+  if (threadIdx.x == 0) st_release_sys(reinterpret_cast<unsigned long long*>(a.peers[dst]) + a.rank, e);
 
   // 2. wait until every rank has published epoch e here (bounded)
   if (threadIdx.x < a.world) {
     const unsigned long long t0 = global_timer_ns();
     for (uint32_t it = 1; ld_acquire_sys(flags + threadIdx.x) < e; ++it) {
-      if ((it & 63u) == 0u && global_timer_ns() - t0 > kWaitBudgetNs) {
+      if ((it & 63u) == 0u && global_timer_ns() - t0 > a.wait_budget_ns) {
         flag_device_error(a.err, AICAS_DEVERR_PEER_TIMEOUT);
         timed_out = 1;
         break;
@@ -76,35 +84,55 @@ __global__ void __launch_bounds__(kExchangeThreads) exchange_merge_kernel(const 
   }
   __syncthreads();
 
-  // 3. merge: one warp per (request, head) row
+  // 3. merge this CTA's share of the rows: one thread per (row, 4 columns)
   const float* slots = reinterpret_cast<const float*>(own + kSlotOffset) + (size_t)par * a.world * a.slot_floats;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int bh = warp; bh < nbh; bh += kExchangeThreads / 32) {
+  const int q4 = a.hd / 4;
+  const int rows_per = (nbh + gridDim.x - 1) / gridDim.x;
+  const int r0 = blockIdx.x * rows_per, r1 = min(nbh, r0 + rows_per);
+  for (int u = threadIdx.x; u < (r1 - r0) * q4; u += blockDim.x) {
+    const int bh = r0 + u / q4, c4 = u % q4;
     const int b = bh / a.heads, h = bh % a.heads;
+    float lse[kMaxExchangeRanks];
     float M = -INFINITY;
-    if (!timed_out)
-      for (int r = lane; r < a.world; r += 32) M = fmaxf(M, slots[(size_t)r * a.slot_floats + n_o + bh]);
 #pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-    float L = 0.f;
-    if (M != -INFINITY)
-      for (int r = 0; r < a.world; ++r) L += exp2f(slots[(size_t)r * a.slot_floats + n_o + bh] - M);
-    for (int d = lane; d < a.hd; d += 32) {
-      float O = 0.f;
-      if (M != -INFINITY)
-        for (int r = 0; r < a.world; ++r) {
-          const float* s = slots + (size_t)r * a.slot_floats;
-          O += exp2f(s[n_o + bh] - M) * s[(size_t)bh * a.hd + d];
-        }
-      const float ov = L > 0.f ? O / L : 0.f;
-      static_cast<T*>(a.out)[(int64_t)b * a.o_sb + (int64_t)h * a.o_sh + d] = Elem<T>::from_float(ov);
+    for (int r = 0; r < kMaxExchangeRanks; ++r) {
+      lse[r] = (r < a.world && !timed_out) ? __ldcv(slots + (size_t)r * a.slot_floats + n_o + bh) : -INFINITY;
+      M = fmaxf(M, lse[r]);
     }
-    if (a.lse != nullptr && lane == 0) a.lse[bh] = L > 0.f ? M + log2f(L) : -INFINITY;
+    float L = 0.f;
+    float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int r = 0; r < kMaxExchangeRanks; ++r) {
+        if (r >= a.world) break;
+        const float w = exp2f(lse[r] - M);
+        const float4 o = __ldcv(reinterpret_cast<const float4*>(slots + (size_t)r * a.slot_floats + (size_t)bh * a.hd) + c4);
+        L += w;
+        O.x = fmaf(w, o.x, O.x);
+        O.y = fmaf(w, o.y, O.y);
+        O.z = fmaf(w, o.z, O.z);
+        O.w = fmaf(w, o.w, O.w);
+      }
+    }
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    T* orow = static_cast<T*>(a.out) + (int64_t)b * a.o_sb + (int64_t)h * a.o_sh + 4 * c4;
+    orow[0] = Elem<T>::from_float(O.x * inv);
+    orow[1] = Elem<T>::from_float(O.y * inv);
+    orow[2] = Elem<T>::from_float(O.z * inv);
+    orow[3] = Elem<T>::from_float(O.w * inv);
+    if (a.lse != nullptr && c4 == 0) a.lse[bh] = L > 0.f ? M + log2f(L) : -INFINITY;
   }
 
-  // 4. this call is complete on this rank
+  // 4. the last CTA of this call advances the epoch: this call is complete on this rank
   __syncthreads();
-  if (threadIdx.x == 0) *epoch_word = e;
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(done_word, 1u) == gridDim.x - 1) {
+      *done_word = 0u;
+      *epoch_word = e;
+      __threadfence();
+    }
+  }
 }
 
 }  // namespace
@@ -119,13 +147,13 @@ size_t exchange_buffer_bytes(int world, int batch, int heads, int head_dim) {
 }
 
 cudaError_t launch_exchange_merge(int dtype, const ExchangeArgs& a, cudaStream_t st) {
+  const dim3 grid(a.world), block(kExchangeThreads);
   switch (dtype) {
-    case AICAS_DTYPE_F32: exchange_merge_kernel<float><<<1, kExchangeThreads, 0, st>>>(a); break;
-    case AICAS_DTYPE_F16: exchange_merge_kernel<__half><<<1, kExchangeThreads, 0, st>>>(a); break;
-    case AICAS_DTYPE_BF16: exchange_merge_kernel<__nv_bfloat16><<<1, kExchangeThreads, 0, st>>>(a); break;
+    case AICAS_DTYPE_F32: return launch_pdl(exchange_merge_kernel<float>, grid, block, 0, st, a);
+    case AICAS_DTYPE_F16: return launch_pdl(exchange_merge_kernel<__half>, grid, block, 0, st, a);
+    case AICAS_DTYPE_BF16: return launch_pdl(exchange_merge_kernel<__nv_bfloat16>, grid, block, 0, st, a);
     default: return cudaErrorInvalidValue;
   }
-  return cudaGetLastError();
 }
 
 }  // namespace aicas

@@ -69,6 +69,7 @@ struct FmhaArgs {
   const int32_t* cu_q;
   const int32_t* cu_k;
   int num_seqs;
+  const int32_t* kv_starts;  // causal prefill: optional first valid key per batch row (left padding)
   unsigned int* err;
 };
 
@@ -236,6 +237,7 @@ __global__ void __launch_bounds__(threads_for<KT>(), 3 - KT) fmha_fwd_kernel(con
 
   // ---------------------------------------------------------------- work unit
   int b = 0, head0, head1, kvh, row0, row1, q_base = 0, k_base = 0, q_len, kv_len;
+  int kv_start = 0;  // keys before it are padding (masked), causal prefill only
   if constexpr (!VARLEN) {
     const int L = blockIdx.x;
     const int mb = a.num_m - 1 - L / a.num_units;  // longest causal rows first
@@ -257,6 +259,7 @@ __global__ void __launch_bounds__(threads_for<KT>(), 3 - KT) fmha_fwd_kernel(con
       row1 = row0 + kBM;
     }
     q_len = kv_len = a.seq_q;
+    if (a.kv_starts != nullptr) kv_start = min(max(__ldg(a.kv_starts + b), 0), kv_len);
   } else {
     if (warp == 0) {
       // find (sequence, row block of KT x 128 rows) of this CTA: prefix sums
@@ -315,7 +318,9 @@ __global__ void __launch_bounds__(threads_for<KT>(), 3 - KT) fmha_fwd_kernel(con
   }
   int kv_end = kv_len;
   if (CAUSAL) kv_end = min(kv_len, max(row0, row1) + kBM);
-  const int n_kv = (kv_end + kBN - 1) / kBN;
+  // key tiles [j0, j0 + n_kv): the ones between the first valid key and the causal end
+  const int j0 = kv_start / kBN;
+  const int n_kv = max(0, (kv_end + kBN - 1) / kBN - j0);
 
   // ---------------------------------------------------------------- set-up
   if (threadIdx.x == 0) {
@@ -383,7 +388,7 @@ __global__ void __launch_bounds__(threads_for<KT>(), 3 - KT) fmha_fwd_kernel(con
           mbar_arrive_expect_tx(kv_full(s), Lay::kKVTile);
           for (int bx = 0; bx < D / 64; ++bx)
             tma_tile(sb + Lay::kKV + s * Lay::kKVTile + bx * (kBN * 128), is_v ? &a.tm_v : &a.tm_k,
-                     is_v ? a.v_rows_first : a.k_rows_first, bx * 64, k_base + j * kBN, kvh, b, kv_full(s));
+                     is_v ? a.v_rows_first : a.k_rows_first, bx * 64, k_base + (j0 + j) * kBN, kvh, b, kv_full(s));
           ++issued;
         }
         if (*abort_flag) {  // let our own copies land before the CTA can retire
@@ -547,13 +552,13 @@ __global__ void __launch_bounds__(threads_for<KT>(), 3 - KT) fmha_fwd_kernel(con
       // S(j) is in registers: the tensor core may overwrite it with S(j+1) now
       tc::fence_before_sync();
       mbar_arrive(s_free(t));
-      const int kv0 = j * kBN;
-      const bool mask = (kv0 + kBN > kv_len) || (CAUSAL && kv0 + kBN - 1 > tile_row0);
+      const int kv0 = (j0 + j) * kBN;
+      const bool mask = (kv0 + kBN > kv_len) || (CAUSAL && kv0 + kBN - 1 > tile_row0) || kv0 < kv_start;
       if (mask) {
 #pragma unroll
         for (int i = 0; i < kBN; ++i) {
           const int col = kv0 + i;
-          if (col >= kv_len || (CAUSAL && col > row)) v[i] = masked_bits;
+          if (col >= kv_len || (CAUSAL && col > row) || col < kv_start) v[i] = masked_bits;
         }
       }
       // row maximum of s*c: 4 independent chains of 3-input max
@@ -821,6 +826,7 @@ int run_fmha(const aicas_fmha_params* p, bool varlen, cudaStream_t stream, unsig
   a.seq_kv = p->seq_len_kv;
   a.group = p->num_q_heads / p->num_kv_heads;
   a.scale_log2 = p->sm_scale * 1.4426950408889634f;
+  a.kv_starts = varlen ? nullptr : p->kv_starts;
   a.err = dev_err;
   long long grid;
   if (varlen) {

@@ -82,6 +82,18 @@ def _call_in_device(device: torch.device, fn, *args):
     return fn(*args)
 
 
+def _reset_workspaces() -> None:
+    """Zero-fills every workspace of this module (after a device error: a kernel
+    whose bounded wait gave up may have left split counters behind)."""
+    for (dev, _), ws in list(_WORKSPACES.items()) + list(_LINEAR_WORKSPACES.items()):
+        with torch.cuda.device(dev):
+            ws.zero_()
+            torch.cuda.synchronize(dev)
+
+
+nat.add_device_error_hook(_reset_workspaces)
+
+
 def _workspace(device: torch.device, stream: int, nbytes: int) -> torch.Tensor:
     key = (device.index, stream)
     ws = _WORKSPACES.get(key)
@@ -133,7 +145,8 @@ def _check_decode(query, key, value, num_key_value_groups: int) -> None:
         raise ValueError("query, key and value dtypes differ")
 
 
-def _decode_call(query, key, value, *, sm_scale, num_key_value_groups, kv_lens, split_tokens, out, lse, partial_o):
+def _decode_call(query, key, value, *, sm_scale, num_key_value_groups, kv_lens, split_tokens, out, lse, partial_o,
+                 kv_starts=None):
     B, Hq, _, D = query.shape
     Hkv, L = key.shape[1], key.shape[2]
     device = query.device
@@ -143,6 +156,7 @@ def _decode_call(query, key, value, *, sm_scale, num_key_value_groups, kv_lens, 
     p.lse = _ptr(lse)
     p.partial_o = _ptr(partial_o)
     p.kv_lens = _ptr(kv_lens)
+    p.kv_starts = _ptr(kv_starts)
     p.q_stride_b, p.q_stride_h = query.stride(0), query.stride(1)
     p.k_stride_b, p.k_stride_h = key.stride(0), key.stride(1)
     p.v_stride_b, p.v_stride_h = value.stride(0), value.stride(1)
@@ -175,15 +189,18 @@ def gqa_decode_attention(
     kv_lens: torch.Tensor | Sequence[int] | None = None,
     return_lse: bool = False,
     split_tokens: int = 0,
+    kv_starts: torch.Tensor | Sequence[int] | None = None,
 ):
     """q_len == 1 GQA attention: softmax(sm_scale * q K^T) V per request.
 
     query ``[B, Hq, 1, D]``, key/value ``[B, Hkv, L, D]`` -> ``[B, Hq, 1, D]``
     (gqa_decode_attention.py:413-430).  Extension: ``kv_lens`` (int32 ``[B]`` on
     the device) limits request ``b`` to its first ``kv_lens[b]`` cache slots, so
-    a padded preallocated cache needs no slicing and no host synchronisation.
-    With ``return_lse`` the base-2 log-sum-exp ``[B, Hq]`` is returned too
-    (the ``lse`` of gqa_decode_attention.py:141).
+    a padded preallocated cache needs no slicing and no host synchronisation;
+    ``kv_starts`` (int32 ``[B]``) skips the first ``kv_starts[b]`` slots (the
+    padding of a left-padded batch).  With ``return_lse`` the base-2
+    log-sum-exp ``[B, Hq]`` is returned too (the ``lse`` of
+    gqa_decode_attention.py:141).
     """
     _reject_grad(query, key, value)
     _check_decode(query, key, value, num_key_value_groups)
@@ -192,10 +209,11 @@ def gqa_decode_attention(
     key = _rows_ready(key)
     value = _rows_ready(value)
     lens = _as_lens(kv_lens, B, query.device)
+    starts = _as_lens(kv_starts, B, query.device)
     out = torch.empty((B, 1, Hq, D), dtype=query.dtype, device=query.device).transpose(1, 2)
     lse = torch.empty((B, Hq), dtype=torch.float32, device=query.device) if return_lse else None
     _decode_call(query, key, value, sm_scale=sm_scale, num_key_value_groups=num_key_value_groups, kv_lens=lens,
-                 split_tokens=split_tokens, out=out, lse=lse, partial_o=None)
+                 split_tokens=split_tokens, out=out, lse=lse, partial_o=None, kv_starts=starts)
     return (out, lse) if return_lse else out
 
 
@@ -393,10 +411,15 @@ def gqa_flash_attention(
     causal: bool,
     sm_scale: float,
     num_key_value_groups: int,
+    kv_starts: torch.Tensor | Sequence[int] | None = None,
 ) -> torch.Tensor:
     """Causal GQA prefill, q_len == kv_len (gqa_flash_attention.py:254-282), on the
     tcgen05 tensor cores.  Returns ``[B, Hq, S, D]`` whose memory is laid out as
-    ``[B, S, Hq, D]``, so the HF backend's transpose back is free."""
+    ``[B, S, Hq, D]``, so the HF backend's transpose back is free.
+
+    Extension: ``kv_starts`` (int32 ``[B]``) masks the first ``kv_starts[b]``
+    positions of batch row ``b`` as keys (a left-padded batch): row ``i`` attends
+    to keys ``[kv_starts[b], i]``, and rows before ``kv_starts[b]`` are zero."""
     if not causal:
         raise ValueError("gqa_flash_attention only supports causal prefill attention.")
     _reject_grad(query, key, value)
@@ -407,10 +430,12 @@ def gqa_flash_attention(
         raise ValueError("gqa_flash_attention needs square causal prefill (q_len == kv_len)")
     B, Hq, S, D = query.shape
     query, key, value = _heads_ready(query), _heads_ready(key), _heads_ready(value)
+    starts = _as_lens(kv_starts, B, query.device)
     out = torch.empty((B, S, Hq, D), dtype=query.dtype, device=query.device).transpose(1, 2)
     if S == 0:
         return out
     p = _fmha_params(query, key, value, out, sm_scale)
+    p.kv_starts = _ptr(starts)
 
     def run():
         nat.check(nat.lib().aicas_prefill_gqa_causal(ctypes.byref(p), _stream_handle(query.device)),

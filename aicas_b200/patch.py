@@ -23,11 +23,13 @@ def _load_attention_registries():
     return ALL_ATTENTION_FUNCTIONS, ALL_MASK_ATTENTION_FUNCTIONS
 
 
-def _set_attr_if_present(target: Any, attr_name: str, value: str) -> bool:
-    if target is None or not hasattr(target, attr_name):
-        return False
-    setattr(target, attr_name, value)
-    return True
+def _switch_backend(config: Any, key: str) -> bool:
+    """Points one config object's ``_attn_implementation`` at ``key``; False
+    (and nothing changed) when the model has no such config object."""
+    has_field = config is not None and hasattr(config, "_attn_implementation")
+    if has_field:
+        config._attn_implementation = key
+    return has_field
 
 
 def install_qwen3vl_triton_attention(model: Any, fuse_vision_rope: bool = False) -> dict[str, Any]:
@@ -51,18 +53,10 @@ def install_qwen3vl_triton_attention(model: Any, fuse_vision_rope: bool = False)
     language_model = getattr(base_model, "language_model", None)
     model_config = getattr(model, "config", None)
     mutated = {
-        "model.model.visual.config": _set_attr_if_present(
-            getattr(visual, "config", None), "_attn_implementation", VISION_BACKEND_KEY
-        ),
-        "model.model.language_model.config": _set_attr_if_present(
-            getattr(language_model, "config", None), "_attn_implementation", TEXT_BACKEND_KEY
-        ),
-        "model.config.vision_config": _set_attr_if_present(
-            getattr(model_config, "vision_config", None), "_attn_implementation", VISION_BACKEND_KEY
-        ),
-        "model.config.text_config": _set_attr_if_present(
-            getattr(model_config, "text_config", None), "_attn_implementation", TEXT_BACKEND_KEY
-        ),
+        "model.model.visual.config": _switch_backend(getattr(visual, "config", None), VISION_BACKEND_KEY),
+        "model.model.language_model.config": _switch_backend(getattr(language_model, "config", None), TEXT_BACKEND_KEY),
+        "model.config.vision_config": _switch_backend(getattr(model_config, "vision_config", None), VISION_BACKEND_KEY),
+        "model.config.text_config": _switch_backend(getattr(model_config, "text_config", None), TEXT_BACKEND_KEY),
     }
     available = _native.available()
     extra = {}

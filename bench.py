@@ -140,6 +140,18 @@ class ClockSampler:
 # ------------------------------------------------------------------ distributed helpers
 
 
+def pin_host_cores(local: int, world: int) -> None:
+    """One disjoint slice of this process's allowed host cores per local rank,
+    so the ranks' Python threads (which issue every launch and copy of the
+    end-to-end step) do not compete for the same cores."""
+    cores = sorted(os.sched_getaffinity(0))
+    per = len(cores) // world
+    if per >= 1:
+        mine = cores[local * per:(local + 1) * per]
+        os.sched_setaffinity(0, mine)
+        torch.set_num_threads(len(mine))
+
+
 def dist_info():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -175,6 +187,18 @@ def step_bytes(lengths: torch.Tensor, layers: int = LAYERS) -> dict:
     qo = 2 * B * hq * d * e                                         # decode reads q, writes o
     rope = B * (hq + 2 * hkv) * d * e + 2 * B * d * e + B * hq * d * e + 2 * B * hkv * d * e
     return {"decode_per_layer": kv + qo, "rope_per_layer": rope, "step": layers * (kv + qo + rope)}
+
+
+def cfg2_config(world: int, layers: int = LAYERS) -> dict:
+    """The headline workload's ``config``, printed identically by both arms."""
+    from aicas_b200 import workloads as wl
+
+    lengths = wl.cfg2_lengths(0)
+    return {"workload": f"cfg2: batched GQA decode step (RoPE + KV append + decode) x {layers} layers",
+            "batch_per_gpu": B, "layers": layers, "q_heads": 16, "kv_heads": 8, "head_dim": 128,
+            "kv_capacity": L_CAP, "lengths": "U[256,4096] seed 0", "mean_len": round(float(lengths.float().mean()), 2),
+            "parallelism": f"dp{world} (requests sharded, no collective)",
+            "l2": "inputs larger than L2 (571 MB of valid KV per layer)"}
 
 
 class DecodeWorkload:
@@ -291,14 +315,8 @@ def run_decode(args, world, rank, device, peaks, peak_src) -> dict:
     del graph, graph_ev
     e2e = run_e2e(wk, args, world, device) if args.e2e else None
     out = {
-        "value": round(value, 1), "ms_per_step": round(ms_step, 4),
-        "config": {"workload": f"cfg2: batched GQA decode step (RoPE + KV append + split-KV decode) x {wk.layers} layers",
-                   "batch_per_gpu": B, "layers": wk.layers, "q_heads": 16, "kv_heads": 8, "head_dim": 128,
-                   "kv_capacity": L_CAP, "lengths": "U[256,4096] seed 0",
-                   "mean_len": round(float(wk.lengths.float().mean()), 2),
-                   "parallelism": f"dp{world} (requests sharded, no collective)",
-                   "l2": "inputs larger than L2 (571 MB of valid KV per layer)",
-                   "graph": f"{wk.layers}-layer step captured in one CUDA graph ({2 * wk.layers} launches)"},
+        "value": round(value, 1), "ms_per_step": round(ms_step, 4), "config": cfg2_config(world, wk.layers),
+        "execution": f"{wk.layers}-layer step captured in one CUDA graph ({2 * wk.layers} launches), replayed",
         "roofline": roofline, "gpu_launches": args.steps * wk.layers * 2, "clocks": clocks.summary(),
     }
     if e2e is not None:
@@ -392,59 +410,163 @@ def run_e2e(wk: DecodeWorkload, args, world, device) -> dict:
     t0 = time.perf_counter()
     for _ in range(steps):
         one_step()
+    issued = time.perf_counter()
     torch.cuda.synchronize(device)
     ms = (time.perf_counter() - t0) * 1e3 / steps
+    host_ms = (issued - t0) * 1e3 / steps
     ms = max_over_ranks(ms, world, device)
+    host_ms = max_over_ranks(host_ms, world, device)
     return {"value": round(world * wk.bytes["step"] / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
             "ms_per_step": round(ms, 4), "steps": steps, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "host_issue_ms_per_step": round(host_ms, 4),
             "api": "aicas_b200.rope_kv_append + backends.text_triton_attention (HF attention interface), eager",
             "timing": "wall clock around the step loop, device synchronised; copies on a copy stream",
-            "h2d_copies_per_step": len(spans), "d2h_copies_per_step": wk.layers}
+            "h2d_copies_per_step": len(spans), "d2h_copies_per_step": wk.layers,
+            "host_cores": len(os.sched_getaffinity(0))}
+
+
+CFG5_B, CFG5_L, CFG5_CHUNK = 4, 131072, 16384
+
+
+def cfg5_shard(s0: int, s1: int, device) -> tuple[torch.Tensor, torch.Tensor]:
+    """Positions [s0, s1) of config 5's K and V ([4, 8, L, 128] bf16).  The whole
+    cache is defined chunk by chunk (16384 positions, chunk c drawn from seed
+    5000 + c), so it is the same for every rank count and a rank generates
+    only the chunks its shard touches."""
+    from aicas_b200 import workloads as wl
+
+    ks, vs = [], []
+    for c in range(s0 // CFG5_CHUNK, (s1 + CFG5_CHUNK - 1) // CFG5_CHUNK):
+        g = wl.generator(5000 + c, device)
+        k = wl.randn((CFG5_B, 8, CFG5_CHUNK, 128), g, torch.bfloat16, device)
+        v = wl.randn((CFG5_B, 8, CFG5_CHUNK, 128), g, torch.bfloat16, device)
+        lo, hi = max(s0 - c * CFG5_CHUNK, 0), min(s1 - c * CFG5_CHUNK, CFG5_CHUNK)
+        ks.append(k[:, :, lo:hi])
+        vs.append(v[:, :, lo:hi])
+    return torch.cat(ks, 2).contiguous(), torch.cat(vs, 2).contiguous()
+
+
+def cfg5_reference(q: torch.Tensor, device) -> torch.Tensor:
+    """fp32 decode over the whole config-5 cache: softmax(scale q K^T) V per
+    (request, query head), [4, 16, 128] fp32, computed one request at a time."""
+    from aicas_b200 import workloads as wl
+
+    k, v = cfg5_shard(0, CFG5_L, device)
+    out = torch.empty(CFG5_B, 16, 128, dtype=torch.float32, device=device)
+    for b in range(CFG5_B):
+        kb, vb = k[b].float(), v[b].float()                       # [8, L, 128]
+        qb = q[b, :, 0].float().view(8, 2, 128)                   # query heads 2h, 2h+1 read KV head h
+        p = torch.softmax(torch.einsum("hgd,hkd->hgk", qb, kb) * wl.SCALE_TEXT, dim=-1)
+        out[b] = torch.einsum("hgk,hkd->hgd", p, vb).reshape(16, 128)
+    return out
+
+
+def _parity(out: torch.Tensor, ref: torch.Tensor, world: int, device) -> dict:
+    """max-abs / mean-abs of every rank's merged output against the fp32
+    reference (max over ranks), held to the north-star bf16 bar."""
+    err = (out.float().reshape(ref.shape) - ref).abs()
+    stats = torch.tensor([float(err.max()), float(err.mean()), float(torch.isfinite(out.float()).all() == 0)],
+                         dtype=torch.float64, device=device)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    mx, mean, nonfinite = (float(x) for x in stats.tolist())
+    return {"max_abs": round(mx, 6), "mean_abs": round(mean, 7), "tolerance": {"max_abs": 2e-2, "mean_abs": 2e-3},
+            "ok": bool(nonfinite == 0 and mx <= 2e-2 and mean <= 2e-3), "against": "fp32 torch over the whole cache"}
 
 
 def run_split_kv(args, world, rank, device) -> dict:
     """Config 5: B=4, L=131072 sequence-sharded over the ranks (strong scaling).
     At N > 1 the partials are exchanged and merged by the one-kernel NVLink
-    peer exchange; the NCCL all-gather + merge path is timed beside it."""
+    peer exchange; the NCCL all-gather + merge path is timed beside it.  Both
+    are checked once, outside the timed loops, against an fp32 decode of the
+    whole cache; the call is timed eagerly and replayed from a CUDA graph, with
+    its decode and exchange kernels timed apart and its host issue time."""
     import aicas_b200 as ab
     from aicas_b200 import distributed as adist
+    from aicas_b200 import ops
     from aicas_b200 import workloads as wl
 
-    Bq, L = 4, 131072
+    Bq, L = CFG5_B, CFG5_L
     s0, s1 = adist.shard_bounds(L, world, rank)
-    g = wl.generator(5, device)
-    q = wl.randn((Bq, 16, 1, 128), g, torch.bfloat16, device)
-    k = wl.randn((Bq, 8, s1 - s0, 128), g, torch.bfloat16, device)
-    v = wl.randn((Bq, 8, s1 - s0, 128), g, torch.bfloat16, device)
+    q = wl.randn((Bq, 16, 1, 128), wl.generator(5, device), torch.bfloat16, device)
+    k, v = cfg5_shard(s0, s1, device)
     exchange = adist.PeerExchange(Bq, 16, 128, device) if world > 1 else None
+    iters = max(10, min(200, args.steps))
 
-    def timed(once) -> float:
+    def timed(once) -> tuple[float, float]:
+        """(device ms per call, max over ranks; host ms to issue one call)"""
         for _ in range(max(args.warmup, 3)):
             once()
         barrier(world, device)
-        iters = max(10, min(200, args.steps))
         st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         st.record()
+        t0 = time.perf_counter()
         for _ in range(iters):
             once()
+        host = (time.perf_counter() - t0) * 1e3 / iters
         en.record()
         torch.cuda.synchronize(device)
-        return max_over_ranks(st.elapsed_time(en) / iters, world, device)
+        return max_over_ranks(st.elapsed_time(en) / iters, world, device), max_over_ranks(host, world, device)
 
+    def in_graph(once):
+        """`once` captured in a CUDA graph (warmed up on the capture stream first,
+        so that its workspace exists before the capture)."""
+        s = torch.cuda.Stream(device)
+        s.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(s):
+            for _ in range(3):
+                once()
+        torch.cuda.current_stream(device).wait_stream(s)
+        torch.cuda.synchronize(device)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            once()
+        return g
+
+    kw = dict(sm_scale=wl.SCALE_TEXT, num_key_value_groups=2)
+    ref = cfg5_reference(q, device) if rank == 0 else torch.empty(Bq, 16, 128, device=device)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.broadcast(ref, src=0)
     kv_bytes = 2 * Bq * 8 * L * 128 * 2
+    base = {"scaling": "strong", "batch": Bq, "kv_len": L, "per_gpu_kv_len": s1 - s0,
+            "data": "seeded N(0,1) chunks of 16384 positions, the same whole cache at every rank count"}
     if world == 1:
-        ms = timed(lambda: ab.gqa_decode_attention(q, k, v, sm_scale=wl.SCALE_TEXT, num_key_value_groups=2))
-        return {"value": round(kv_bytes / (ms * 1e-3) / 1e9, 1), "unit": "GB/s", "ms_per_call": round(ms, 4),
-                "scaling": "strong", "batch": Bq, "kv_len": L, "per_gpu_kv_len": s1 - s0, "collective": "none"}
-    ms = timed(lambda: adist.sharded_gqa_decode(q, k, v, sm_scale=wl.SCALE_TEXT, num_key_value_groups=2,
-                                                exchange=exchange))
-    ms_nccl = timed(lambda: adist.sharded_gqa_decode(q, k, v, sm_scale=wl.SCALE_TEXT, num_key_value_groups=2))
+        decode = lambda: ab.gqa_decode_attention(q, k, v, **kw)  # noqa: E731
+        parity = _parity(decode(), ref, world, device)
+        ms_eager, host = timed(decode)
+        g = in_graph(decode)
+        ms, _ = timed(g.replay)
+        del g
+        return {**base, "value": round(kv_bytes / (ms * 1e-3) / 1e9, 1), "unit": "GB/s", "ms_per_call": round(ms, 4),
+                "eager_ms_per_call": round(ms_eager, 4), "host_ms_per_call": round(host, 4), "collective": "none",
+                "timing": "CUDA-graph replays of the call (eager beside it)", "parity": parity}
+
+    peer = lambda: adist.sharded_gqa_decode(q, k, v, exchange=exchange, **kw)  # noqa: E731
+    nccl = lambda: adist.sharded_gqa_decode(q, k, v, **kw)  # noqa: E731
+    parity = {"peer": _parity(peer(), ref, world, device), "nccl": _parity(nccl(), ref, world, device)}
+    ms_eager, host = timed(peer)
+    po, lse = ops.gqa_decode_partial(q, k, v, **kw)
+    ms_decode, _ = timed(lambda: ops.gqa_decode_partial(q, k, v, **kw))
+    ms_exchange, host_exchange = timed(lambda: exchange.merge(po, lse, q.dtype))
+    g = in_graph(peer)
+    ms, _ = timed(g.replay)
+    del g
+    ms_nccl, _ = timed(nccl)
+    torch.cuda.synchronize(device)
     exchange.close()
-    return {"value": round(kv_bytes / (ms * 1e-3) / 1e9, 1), "unit": "GB/s", "ms_per_call": round(ms, 4),
-            "scaling": "strong", "batch": Bq, "kv_len": L, "per_gpu_kv_len": s1 - s0,
-            "collective": "NVLink peer-memory exchange + merge in one kernel (CUDA IPC buffers)",
+    return {**base, "value": round(kv_bytes / (ms * 1e-3) / 1e9, 1), "unit": "GB/s", "ms_per_call": round(ms, 4),
+            "timing": "CUDA-graph replays of the sharded call (partial decode + peer exchange kernel)",
+            "collective": "NVLink peer-memory exchange + merge in one kernel (CUDA IPC buffers, one CTA per peer)",
+            "breakdown_ms": {"eager_call": round(ms_eager, 4), "host_issue_per_eager_call": round(host, 4),
+                             "partial_decode": round(ms_decode, 4), "exchange_merge": round(ms_exchange, 4),
+                             "host_issue_per_exchange": round(host_exchange, 4)},
             "nccl_all_gather_path": {"value": round(kv_bytes / (ms_nccl * 1e-3) / 1e9, 1),
-                                     "ms_per_call": round(ms_nccl, 4)}}
+                                     "ms_per_call": round(ms_nccl, 4), "timing": "eager"},
+            "parity": parity}
 
 
 def run_fmha_secondary(args, world, device, peaks, only=None) -> dict:
@@ -628,27 +750,46 @@ def run_generate(device) -> dict:
 
 def cpu_decode_sample(target_s: float, max_layers: int = 100000) -> dict:
     """Times the reference's CPU path (oracle/reference_cpu.py) on whole config-2
-    layers (all 64 requests) on the host cores; returns GB/s of the same metric."""
+    layers (all 64 requests) on the host cores, layer after layer of the step
+    (each with its own inputs, the distinct layer caches in rotation, as the
+    reference arm runs them); returns GB/s of the same metric."""
     from aicas_b200 import workloads as wl
     from oracle import reference_cpu as rc
 
-    torch.set_num_threads(os.cpu_count() or 1)
+    torch.set_num_threads(len(os.sched_getaffinity(0)))
     lengths = wl.cfg2_lengths(0)
     per_layer = step_bytes(lengths)["step"] / LAYERS
-    kc, vc = wl.cfg2_cache(B, L_CAP, 0, seed=0)
-    x = wl.cfg2_step_inputs(lengths, 0, seed=0)
-    rc.decode_layer(x.q, x.k, x.v, x.cos, x.sin, kc, vc, x.positions, wl.SCALE_TEXT)  # warm-up
+    caches = [wl.cfg2_cache(B, L_CAP, layer, seed=0) for layer in range(REF_DISTINCT_CACHES)]
+    inputs = [wl.cfg2_step_inputs(lengths, layer, seed=0) for layer in range(LAYERS)]
+
+    def layer_call(i):
+        x, (kc, vc) = inputs[i % LAYERS], caches[i % REF_DISTINCT_CACHES]
+        rc.decode_layer(x.q, x.k, x.v, x.cos, x.sin, kc, vc, x.positions, wl.SCALE_TEXT)
+
+    layer_call(0)  # warm-up
     layers, t0 = 0, time.perf_counter()
     while layers < max_layers and (layers == 0 or time.perf_counter() - t0 < target_s):
-        rc.decode_layer(x.q, x.k, x.v, x.cos, x.sin, kc, vc, x.positions, wl.SCALE_TEXT)
+        layer_call(layers)
         layers += 1
     dt = time.perf_counter() - t0
     return {"value": round(layers * per_layer / dt / 1e9, 3), "unit": "GB/s", "cores": torch.get_num_threads(),
             "kind": "port", "seconds": round(dt, 2),
-            "sample": f"{layers} x one config-2 layer (64 requests, RoPE + append + per-request SDPA) on CPU"}
+            "sample": f"{layers} config-2 layer calls in step order (64 requests each: RoPE + append + per-request "
+                      f"SDPA) on CPU, {REF_DISTINCT_CACHES} distinct layer caches in rotation"}
+
+
+# distinct layer caches the reference arm rotates through: 4 x 1.07 GB of host
+# memory (28 would be 30 GB); each layer reads 591 MB of valid K/V, so the
+# rotation period (2.4 GB) is far larger than any CPU's last-level cache and
+# the CPU gets no reuse from one layer to the next
+REF_DISTINCT_CACHES = 4
 
 
 def run_reference(args, world, rank) -> dict | None:
+    """The reference's own CPU path (oracle/reference_cpu.py restates it; the
+    reference is Python and cannot travel) on the host cores, on the same
+    config-2 step: 28 layers, each with its own step inputs, over distinct
+    layer caches.  Imports no native code."""
     if rank != 0:
         return None
     from aicas_b200 import workloads as wl
@@ -657,10 +798,12 @@ def run_reference(args, world, rank) -> dict | None:
     torch.set_num_threads(os.cpu_count() or 1)
     lengths = wl.cfg2_lengths(0)
     per_layer = step_bytes(lengths)["step"] / LAYERS
-    kc, vc = wl.cfg2_cache(B, L_CAP, 0, seed=0)
-    x = wl.cfg2_step_inputs(lengths, 0, seed=0)
+    caches = [wl.cfg2_cache(B, L_CAP, layer, seed=0) for layer in range(REF_DISTINCT_CACHES)]
+    inputs = [wl.cfg2_step_inputs(lengths, layer, seed=0) for layer in range(LAYERS)]
+
     def one_step():
-        for _ in range(LAYERS):
+        for layer, x in enumerate(inputs):
+            kc, vc = caches[layer % REF_DISTINCT_CACHES]
             rc.decode_layer(x.q, x.k, x.v, x.cos, x.sin, kc, vc, x.positions, wl.SCALE_TEXT)
 
     for _ in range(args.warmup):
@@ -670,14 +813,15 @@ def run_reference(args, world, rank) -> dict | None:
         one_step()
     dt = time.perf_counter() - t0
     value = args.steps * LAYERS * per_layer / dt / 1e9
-    sample = ("one config-2 step per step: 28 layer calls (64 requests each: RoPE + cache append + per-request "
-              "SDPA, bf16) on CPU, layer 0's caches reused for every layer")
+    sample = (f"one config-2 step per step: 28 layer calls (64 requests each: RoPE + cache append + per-request "
+              f"SDPA, bf16) on CPU, each layer with its own inputs, {REF_DISTINCT_CACHES} distinct layer caches "
+              "in rotation")
     return {
         "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(dt * 1e3 / args.steps, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "impl": "reference",
-        "config": {"workload": "cfg2: batched GQA decode step (RoPE + KV append + decode) x 28 layers, reference CPU path",
-                   "batch": B, "kv_capacity": L_CAP, "lengths": "U[256,4096] seed 0"},
+        "config": cfg2_config(world),
+        "execution": "reference CPU path (torch CPU operators), all host threads",
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
                          "sample": sample},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -743,6 +887,8 @@ def _main(out: "_JsonStdout", argv=None) -> int:
 
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    if world > 1 and os.environ.get("AICAS_BENCH_NO_PIN") is None:
+        pin_host_cores(local, world)
     if world > 1:
         import torch.distributed as dist
 
@@ -770,7 +916,8 @@ def _main(out: "_JsonStdout", argv=None) -> int:
         dec = result.pop("decode", None)
         if dec is not None:
             line.update({"value": dec["value"], "unit": "GB/s", "ms_per_step": dec["ms_per_step"], "scaling": "weak",
-                         "config": dec["config"], "roofline": dec["roofline"], "e2e": dec.get("e2e"),
+                         "config": dec["config"], "execution": dec["execution"], "roofline": dec["roofline"],
+                         "e2e": dec.get("e2e"),
                          "gpu_launches": dec["gpu_launches"], "clocks": dec["clocks"]})
         else:
             line.update({"value": None, "unit": None, "note": f"--only {only}: headline decode not run"})
@@ -784,6 +931,11 @@ def _main(out: "_JsonStdout", argv=None) -> int:
         dist.destroy_process_group()
     if line is not None:
         out.emit(line)
+    sk = result.get("split_kv_cfg5", {}).get("parity")
+    checks = ([sk] if "ok" in sk else list(sk.values())) if sk else []
+    if not all(c["ok"] for c in checks):
+        log(f"split-KV parity check FAILED: {sk}")
+        return 1
     return 0
 
 

@@ -71,7 +71,7 @@
 extern "C" {
 #endif
 
-#define AICAS_ABI_VERSION 1
+#define AICAS_ABI_VERSION 2
 
 /* element types */
 #define AICAS_DTYPE_F32 0
@@ -114,6 +114,9 @@ typedef struct aicas_decode_params {
   int32_t split_tokens;    /* tokens per split-KV work unit; 0 = choose automatically (for
                               many (request, KV head) pairs a halving table: the first split
                               of each cache the longest, later ones down to 1/8 of it) */
+  const int32_t* kv_starts; /* optional [B] first valid cache slot per request; request b attends
+                              to slots [kv_starts[b], kv_lens[b]) (a left-padded batch: the
+                              slots before are padding); NULL = 0 */
 } aicas_decode_params;
 
 /* Bytes of device workspace aicas_decode_gqa needs for these parameters (0 when
@@ -138,8 +141,9 @@ AICAS_API int aicas_decode_gqa(const aicas_decode_params* p, void* workspace, si
    the library (held by every GPU that loads it, until exit), enough for about
    7 MiB of partial results (B * Hkv * splits * G * (D + 1) * 4 bytes);
    larger requests are rejected with AICAS_ERR_UNSUPPORTED (raise split_tokens
-   or use aicas_decode_gqa).  The first call on a device looks up the array's
-   device address and should come before any stream capture on that device.
+   or use aicas_decode_gqa).  The first call in a CUDA context looks up the
+   array's device address in that context and should come before any stream
+   capture in it.
    Every call shares the one array and clears the counters it uses on
    `stream` before launching, so calls that may overlap on the device (other
    streams, other host threads) race and must be serialised by the caller. */
@@ -171,9 +175,12 @@ AICAS_API int aicas_merge_partials(const aicas_merge_params* p, void* stream);
 /* 64-byte IPC handle with the other ranks, and maps theirs with              */
 /* aicas_peer_buffer_open.  Each aicas_exchange_merge call is collective: all */
 /* ranks make the same sequence of calls with the same sizes.  A rank waits   */
-/* at most a few seconds for the others, then sets AICAS_DEVERR_PEER_TIMEOUT, */
-/* writes zeros and returns; the buffers are then out of step and must be     */
-/* re-created.                                                               */
+/* at most wait_budget_ns (default 4 s) for the others, then sets             */
+/* AICAS_DEVERR_PEER_TIMEOUT, writes zeros and returns; the buffers are then  */
+/* out of step and must be re-created.  One CTA per rank pushes to each      */
+/* destination in parallel; launched with programmatic dependent launch, so  */
+/* its launch overlaps the end of the decode kernel that produced the        */
+/* partial.                                                                  */
 /* ------------------------------------------------------------------------ */
 #define AICAS_MAX_EXCHANGE_RANKS 8
 #define AICAS_IPC_HANDLE_BYTES 64
@@ -195,6 +202,8 @@ typedef struct aicas_exchange_params {
   int64_t o_stride_b, o_stride_h;
   int32_t world, rank, batch, num_heads, head_dim;
   int32_t dtype;            /* dtype of out */
+  uint64_t wait_budget_ns;  /* how long a rank waits for the others' partials before it gives up
+                               (sets AICAS_DEVERR_PEER_TIMEOUT, writes zeros); 0 = 4 s */
 } aicas_exchange_params;
 
 AICAS_API int aicas_exchange_merge(const aicas_exchange_params* p, void* stream);
@@ -218,6 +227,10 @@ typedef struct aicas_fmha_params {
   const int32_t* cu_seqlens_q; /* varlen only: [num_seqs + 1] int32 on the device */
   const int32_t* cu_seqlens_k; /* varlen only: [num_seqs + 1] int32 on the device */
   int32_t num_seqs;            /* varlen only */
+  const int32_t* kv_starts;    /* causal prefill only, optional: [B] int32 on the device, the first
+                                  valid position of each batch row (a left-padded batch); query row
+                                  i of batch b attends to keys [kv_starts[b], i], rows before
+                                  kv_starts[b] get zeros; NULL = 0 */
 } aicas_fmha_params;
 
 /* q_len == kv_len causal prefill, Hq a multiple of Hkv (gqa_flash_attention.py:12-46). */

@@ -62,6 +62,34 @@ def decode_ragged(q: np.ndarray, k: np.ndarray, v: np.ndarray, lens, scale: floa
     return out
 
 
+def sdpa_padded(q: np.ndarray, k: np.ndarray, v: np.ndarray, mask: np.ndarray, scale: float, groups: int):
+    """The reference's masked text path: backends.py:249-260 (prefill) and
+    277-287 (decode) send a call with a padding mask to sdpa_fallback
+    (fallback.py:23-64), i.e. HF's SDPA with the 4-D mask HF builds from the
+    2-D one: query i (at absolute position i + kv_len - q_len) sees key j when
+    mask[b, j] is nonzero and j <= that position.
+
+    Returns (out [B, Hq, Sq, D], real [B, Sq]): ``real`` marks the query rows at
+    real-token positions, the only rows Hugging Face uses (the outputs at
+    padded positions are discarded; there they are set to 0 here)."""
+    q = q.astype(np.float64)
+    kk = repeat_kv(k.astype(np.float64), groups)
+    vv = repeat_kv(v.astype(np.float64), groups)
+    sq, skv = q.shape[2], kk.shape[2]
+    pos = np.arange(sq) + (skv - sq)
+    allowed = (np.asarray(mask)[:, None, None, :] != 0) & (np.arange(skv)[None, None, None, :] <= pos[None, None, :, None])
+    s = np.einsum("bhqd,bhkd->bhqk", q, kk) * scale
+    s = np.where(allowed, s, -np.inf)
+    real = np.asarray(mask)[:, pos] != 0
+    rows = allowed.any(axis=-1)  # [B, 1, Sq, 1] -> rows with at least one key
+    m = np.where(rows[..., None], s.max(axis=-1, keepdims=True), 0.0)
+    p = np.where(allowed, np.exp(s - m), 0.0)
+    den = p.sum(axis=-1, keepdims=True)
+    out = np.einsum("bhqk,bhkd->bhqd", p / np.where(den > 0, den, 1.0), vv)
+    out = np.where(real[:, None, :, None], out, 0.0)
+    return out, real
+
+
 def varlen(q: np.ndarray, k: np.ndarray, v: np.ndarray, cu_q, cu_k, scale: float) -> np.ndarray:
     """_vision_varlen_fallback (backends.py:41-87): split the packed [1, H, T, D]
     tensors by cu_seqlens and run non-causal attention per segment."""

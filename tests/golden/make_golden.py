@@ -146,6 +146,37 @@ def main() -> int:
     save("cfg3_varlen_small", {"seed": 5, "images": 4, "heads": 2, "lo": 4, "hi": 16, "scale": wl.SCALE_VIT},
          checksum=checksum(q, k, v), cu=cu.numpy(), out=out.numpy())
 
+    # -- padded text batches: the reference's masked path is sdpa_fallback
+    #    (backends.py:249-260, 277-287).  Handed HF's 2-D padding mask (what its
+    #    flash_attention_2 mask mapping gives it) that path raises inside SDPA, so
+    #    it is run here with the 4-D mask HF builds for SDPA: key j visible to
+    #    query i when j is a real token and j <= i's position.  Rows at padded
+    #    query positions are stored but not compared (HF discards them).
+    B, S, hq, hkv, D = 3, 40, 4, 2, 128
+    g = wl.generator(13)
+    mask2d = torch.ones(B, S + 1, dtype=torch.bool)
+    mask2d[1, :7] = False   # left padding
+    mask2d[2, :33] = False  # left padding, 7 real prompt tokens
+    q = wl.randn((B, hq, S, D), g, torch.bfloat16)
+    k = wl.randn((B, hkv, S + 1, D), g, torch.bfloat16)
+    v = wl.randn((B, hkv, S + 1, D), g, torch.bfloat16)
+    qd = wl.randn((B, hq, 1, D), g, torch.bfloat16)
+
+    def four_d(m2, sq, skv):
+        pos = torch.arange(sq) + (skv - sq)
+        return m2[:, None, None, :skv] & (torch.arange(skv)[None, None, None, :] <= pos[None, None, :, None])
+
+    def masked_ref(qq, kk, vv, m4):
+        out, _ = backends.text_triton_attention(Module(2, D ** -0.5, True), qq.float(), kk.float(), vv.float(),
+                                                attention_mask=m4, dropout=0.0, scaling=None)
+        return out.nan_to_num(0.0)
+
+    pre = masked_ref(q, k[:, :, :S], v[:, :, :S], four_d(mask2d[:, :S], S, S))
+    dec = masked_ref(qd, k, v, four_d(mask2d, 1, S + 1))
+    save("padded_text", {"seed": 13, "groups": 2, "scale": D ** -0.5, "seq": S},
+         mask=mask2d.numpy(), q=q.float().numpy(), k=k.float().numpy(), v=v.float().numpy(), q_dec=qd.float().numpy(),
+         out_prefill=pre.numpy(), out_decode=dec.numpy())
+
     # -- text RoPE (+ per-head RMSNorm) exactly as Qwen3VLTextAttention runs it before the backend
     from transformers.models.qwen3_vl.configuration_qwen3_vl import Qwen3VLTextConfig
     from transformers.models.qwen3_vl.modeling_qwen3_vl import (

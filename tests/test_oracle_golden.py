@@ -186,3 +186,18 @@ def test_vision_rope_oracle_bit_exact_against_hf():
     for x, ref in ((q, hq), (k, hk)):
         ours = orope.apply_rope_vision(x.float().numpy(), cos.numpy(), sin.numpy(), "bf16")
         assert np.array_equal(ours, ref.float().numpy())
+
+
+def test_padded_text_oracle_against_the_reference_sdpa_path():
+    """oracle.sdpa_padded restates the reference's masked path (HF SDPA with the
+    4-D padding + causal mask); pinned on the rows HF uses (real query tokens)."""
+    meta, a = load_golden("padded_text")
+    S, mask = meta["seq"], a["mask"]
+    pre, real = oa.sdpa_padded(a["q"], a["k"][:, :, :S], a["v"][:, :, :S], mask[:, :S], meta["scale"], meta["groups"])
+    ref = a["out_prefill"].transpose(0, 2, 1, 3)  # the backend returns [B, S, H, D]
+    rows = real[:, None, :, None] & np.ones_like(pre, dtype=bool)
+    np.testing.assert_allclose(pre[rows], ref[rows], rtol=0, atol=2e-6)
+    assert not real.all() and real.any()
+    dec, real_d = oa.sdpa_padded(a["q_dec"], a["k"], a["v"], mask, meta["scale"], meta["groups"])
+    assert real_d.all()
+    np.testing.assert_allclose(dec, a["out_decode"].transpose(0, 2, 1, 3), rtol=0, atol=2e-6)

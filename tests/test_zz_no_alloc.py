@@ -75,19 +75,20 @@ def test_noalloc_matches_the_workspace_entry_point_on_two_calls(cuda_device, nat
 
 
 def test_noalloc_rejects_requests_beyond_its_static_scratch(cuda_device, native_lib):
+    # real, correctly sized caches (every pointer the call is given stays inside
+    # its allocation): 512 (request, KV head) pairs at capacity 2048 in splits of
+    # 64 tokens need 512 x 32 splits x 2 heads x 129 x 4 B = ~17 MB of partials,
+    # more than the 8 MiB static scratch, so the call is refused while planning
     q = torch.zeros(64, 16, 1, 128, dtype=torch.bfloat16, device=cuda_device)
-    k = torch.zeros(64, 8, 1, 128, dtype=torch.bfloat16, device=cuda_device)
-    lens = torch.full((64,), 1, dtype=torch.int32, device=cuda_device)
+    k = torch.zeros(64, 8, 2048, 128, dtype=torch.bfloat16, device=cuda_device)
+    v = torch.zeros_like(k)
+    lens = torch.full((64,), 2048, dtype=torch.int32, device=cuda_device)
     out = torch.empty_like(q)
-    # a 16384-slot cache (never read: the call is refused while planning):
-    # 512 (request, KV head) pairs x 128 splits of 128 tokens = ~67 MB of partials
-    p = _params(q, k, k, out, lens, 128)
-    p.k_stride_b = p.v_stride_b = 8 * 16384 * 128
-    p.k_stride_h = p.v_stride_h = 16384 * 128
-    p.kv_capacity = 16384
+    p = _params(q, k, v, out, lens, 64)
     rc = native_lib.aicas_decode_gqa_noalloc(ctypes.byref(p), torch.cuda.current_stream(cuda_device).cuda_stream)
     assert rc == nat.ERR_UNSUPPORTED
     assert "static scratch" in nat.last_error()
+    del k, v
 
 
 def test_noalloc_large_batch_takes_whole_caches(cuda_device, native_lib):
