@@ -382,7 +382,7 @@ def run_e2e(wk: DecodeWorkload, args, world, device) -> dict:
     ev_out = [torch.cuda.Event() for _ in range(wk.layers)]
     chunk_of = [next(i for i, (a, b) in enumerate(chunks) if a <= layer < b) for layer in range(wk.layers)]
 
-    def one_step():
+    def one_step(main):
         with torch.cuda.stream(copy):
             copy.wait_stream(main)  # the previous step's readers of the input buffer are done
             for i, (lo, hi) in enumerate(spans):
@@ -399,29 +399,51 @@ def run_e2e(wk: DecodeWorkload, args, world, device) -> dict:
             with torch.cuda.stream(copy):
                 copy.wait_event(ev_out[layer])
                 host_out[layer].copy_(out, non_blocking=True)
-                out.record_stream(copy)
+                keep[layer] = out  # alive until the copy stream has read it
         main.wait_stream(copy)
 
+    keep = [None] * wk.layers
     steps = max(3, min(args.steps, 50))
-    for _ in range(max(args.warmup, 3)):
-        one_step()
+
+    def timed_loop(step) -> tuple[float, float]:
+        for _ in range(max(args.warmup, 3)):
+            step()
+        torch.cuda.synchronize(device)
+        barrier(world, device)
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            step()
+        issued = time.perf_counter()
+        torch.cuda.synchronize(device)
+        ms = (time.perf_counter() - t0) * 1e3 / steps
+        host_ms = (issued - t0) * 1e3 / steps
+        return max_over_ranks(ms, world, device), max_over_ranks(host_ms, world, device)
+
+    main = torch.cuda.current_stream(device)
+    eager_ms, eager_host_ms = timed_loop(lambda: one_step(main))
+    # the same step captured in one CUDA graph, the host copies as graph nodes:
+    # the host then issues one launch per step instead of 56 operator calls
+    cap = torch.cuda.Stream(device)
+    cap.wait_stream(main)
+    with torch.cuda.stream(cap):
+        one_step(cap)
+    main.wait_stream(cap)
     torch.cuda.synchronize(device)
-    barrier(world, device)
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        one_step()
-    issued = time.perf_counter()
-    torch.cuda.synchronize(device)
-    ms = (time.perf_counter() - t0) * 1e3 / steps
-    host_ms = (issued - t0) * 1e3 / steps
-    ms = max_over_ranks(ms, world, device)
-    host_ms = max_over_ranks(host_ms, world, device)
-    return {"value": round(world * wk.bytes["step"] / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
-            "ms_per_step": round(ms, 4), "steps": steps, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "host_issue_ms_per_step": round(host_ms, 4),
-            "api": "aicas_b200.rope_kv_append + backends.text_triton_attention (HF attention interface), eager",
-            "timing": "wall clock around the step loop, device synchronised; copies on a copy stream",
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=cap):
+        one_step(cap)
+    ms, host_ms = timed_loop(graph.replay)
+    del graph
+    gbs = lambda t: round(world * wk.bytes["step"] / (t * 1e-3) / 1e9, 1)  # noqa: E731
+    return {"value": gbs(ms), "unit": "GB/s", "ms_per_step": round(ms, 4), "steps": steps,
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "host_issue_ms_per_step": round(host_ms, 4),
+            "api": "aicas_b200.rope_kv_append + backends.text_triton_attention (HF attention interface)",
+            "timing": "wall clock around the step loop, device synchronised; the step (its pinned-host -> device "
+                      "input copies, 56 operator calls and device -> pinned-host output copies, copies on a copy "
+                      "stream) captured in one CUDA graph and replayed",
             "h2d_copies_per_step": len(spans), "d2h_copies_per_step": wk.layers,
+            "eager": {"value": gbs(eager_ms), "ms_per_step": round(eager_ms, 4),
+                      "host_issue_ms_per_step": round(eager_host_ms, 4)},
             "host_cores": len(os.sched_getaffinity(0))}
 
 
@@ -731,6 +753,172 @@ def run_products(args, world, device, peaks) -> dict:
             "scaling": "weak (replicas)"}
 
 
+# ------------------------------------------------------------------ the reference's own GPU kernels
+
+REF_DIR = REPO / "baseline" / "_ref"
+
+
+def install_reference(src: Path) -> dict:
+    """``--install-reference SRC``: puts the reference's GPU code under
+    baseline/_ref (git-ignored; it travels to the GPU box) for the ``refgpu``
+    comparison leg.  The reference has no package metadata, so the offline pip
+    install is tried first and, when it fails, its ``triton_qwen3vl`` package
+    is copied unmodified; its native decode ops are built by its own setup
+    script (dujunbaoV1/setup_native_cuda_ops.py) for sm_100a in a scratch copy
+    (the source tree may be read-only).  The outcome is written to
+    baseline/_ref/INSTALL.json."""
+    import shutil
+    import subprocess
+    import tempfile
+
+    REF_DIR.mkdir(parents=True, exist_ok=True)
+    rec: dict = {}
+    pip = subprocess.run([sys.executable, "-m", "pip", "install", "--no-index", "--no-build-isolation",
+                          "--find-links", "/opt/wheelhouse", "--target", str(REF_DIR), str(src)],
+                         capture_output=True, text=True)
+    rec["pip_install"] = {"rc": pip.returncode, "tail": (pip.stdout + pip.stderr).strip().splitlines()[-3:]}
+    if not (REF_DIR / "triton_qwen3vl").exists():
+        shutil.copytree(src / "triton_qwen3vl", REF_DIR / "triton_qwen3vl",
+                        ignore=shutil.ignore_patterns("__pycache__"))
+        rec["triton_qwen3vl"] = "copied unmodified (no package metadata for pip)"
+    with tempfile.TemporaryDirectory() as tmp:
+        work = Path(tmp) / "dujunbaoV1"
+        work.mkdir()
+        shutil.copy(src / "dujunbaoV1" / "setup_native_cuda_ops.py", work)
+        shutil.copytree(src / "dujunbaoV1" / "native_cuda_ops", work / "native_cuda_ops",
+                        ignore=shutil.ignore_patterns("__pycache__"))
+        env = dict(os.environ, TORCH_CUDA_ARCH_LIST="10.0a", MAX_JOBS="8")
+        b = subprocess.run([sys.executable, "setup_native_cuda_ops.py", "build_ext", "--inplace"], cwd=work,
+                           capture_output=True, text=True, env=env)
+        rec["native_cuda_ops_build"] = {"rc": b.returncode, "arch": "sm_100a (TORCH_CUDA_ARCH_LIST=10.0a)",
+                                        "tail": (b.stdout + b.stderr).strip().splitlines()[-3:]}
+        if b.returncode == 0:
+            dst = REF_DIR / "native_cuda_ops"
+            if dst.exists():
+                shutil.rmtree(dst)
+            shutil.copytree(work / "native_cuda_ops", dst, ignore=shutil.ignore_patterns("__pycache__", "*.o"))
+    (REF_DIR / "INSTALL.json").write_text(json.dumps(rec, indent=1))
+    return rec
+
+
+def _load_ref_package(name: str, alias: str):
+    """The reference package ``name`` from baseline/_ref under ``alias`` (this
+    repository's own drop-in shim already owns the name triton_qwen3vl)."""
+    import importlib.util
+
+    root = REF_DIR / name
+    if alias in sys.modules:
+        return sys.modules[alias]
+    spec = importlib.util.spec_from_file_location(alias, root / "__init__.py", submodule_search_locations=[str(root)])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[alias] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def run_refgpu(args, world, device, peaks) -> dict:
+    """The reference's own GPU kernels on this B200, beside this repository's
+    on the same inputs (timing only; each call timed alone after an L2 flush):
+    its Triton GQA decode (per-request calls over config 2's ragged valid
+    prefixes, and one padded launch at their mean length), its Triton causal
+    prefill (config 4) and varlen ViT attention (config 3), and its native fp16
+    decode_q1_gqa kernel at the shapes it supports (head_dim 128, <= 1024
+    cached tokens)."""
+    import aicas_b200 as ab
+    from aicas_b200 import workloads as wl
+
+    if not (REF_DIR / "triton_qwen3vl").exists():
+        return {"unavailable": "baseline/_ref has no reference install (run bench.py --install-reference SRC)"}
+    ref = _load_ref_package("triton_qwen3vl", "ref_triton_qwen3vl")
+    import ref_triton_qwen3vl.gqa_decode_attention as rdec  # noqa: F401  (submodules of the alias)
+    out: dict = {"source": "baseline/_ref (the reference's triton_qwen3vl, unmodified)"}
+
+    def pair(ref_ms, ours_ms, work, unit):
+        return {"reference_ms": round(ref_ms, 4), "ours_ms": round(ours_ms, 4), "speedup": round(ref_ms / ours_ms, 2),
+                "reference_" + unit: round(work / (ref_ms * 1e-3) / (1e9 if unit == "gbs" else 1e12), 1),
+                "ours_" + unit: round(work / (ours_ms * 1e-3) / (1e9 if unit == "gbs" else 1e12), 1)}
+
+    # ---- decode, config 2, one layer
+    lengths = wl.cfg2_lengths(0)
+    kc, vc = wl.cfg2_cache(B, L_CAP, 0, seed=0, device=device)
+    q = wl.randn((B, 16, 1, 128), wl.generator(3, device), torch.bfloat16, device)
+    lens_dev = lengths.to(device)
+    layer_bytes = sum(2 * 8 * 128 * 2 * int(n) for n in lengths) + 2 * B * 16 * 128 * 2
+    per_req = [(kc[b:b + 1, :, :int(n)].contiguous(), vc[b:b + 1, :, :int(n)].contiguous()) for b, n in enumerate(lengths)]
+
+    def ref_loop():
+        for b, (kb, vb) in enumerate(per_req):
+            ref.gqa_decode_attention(q[b:b + 1], kb, vb, sm_scale=wl.SCALE_TEXT, num_key_value_groups=2)
+
+    ours = lambda: ab.gqa_decode_attention(q, kc, vc, sm_scale=wl.SCALE_TEXT, num_key_value_groups=2,  # noqa: E731
+                                           kv_lens=lens_dev)
+    out["decode_cfg2_ragged"] = {**pair(_time_calls(ref_loop, 10, 3, world, device), _time_calls(ours, 20, 3, world, device),
+                                        layer_bytes, "gbs"),
+                                 "reference_call": "64 gqa_decode_attention calls, one per request over its valid prefix "
+                                                   "(the reference has no length vector)",
+                                 "ours_call": "one gqa_decode_attention call with kv_lens"}
+    del per_req
+    mean_len = int(lengths.float().mean())
+    ku, vu = kc[:, :, :mean_len].contiguous(), vc[:, :, :mean_len].contiguous()
+    uni_bytes = 2 * B * 8 * mean_len * 128 * 2 + 2 * B * 16 * 128 * 2
+    out["decode_uniform_mean_len"] = {
+        **pair(_time_calls(lambda: ref.gqa_decode_attention(q, ku, vu, sm_scale=wl.SCALE_TEXT, num_key_value_groups=2),
+                           20, 3, world, device),
+               _time_calls(lambda: ab.gqa_decode_attention(q, ku, vu, sm_scale=wl.SCALE_TEXT, num_key_value_groups=2),
+                           20, 3, world, device), uni_bytes, "gbs"),
+        "shape": f"B64 Hq16 Hkv8 L{mean_len} D128 bf16 (config 2's mean length, every request)"}
+    del ku, vu, kc, vc
+
+    # ---- prefill, config 4, and ViT varlen, config 3
+    qp, kp, vp = wl.cfg4_prefill(seed=0, device=device)
+    flops = 2 * 8 * 16 * 2048 * 2048 * 128
+    out["prefill_cfg4"] = pair(
+        _time_calls(lambda: ref.gqa_flash_attention(qp, kp, vp, causal=True, sm_scale=wl.SCALE_TEXT,
+                                                    num_key_value_groups=2), 10, 3, world, device),
+        _time_calls(lambda: ab.gqa_flash_attention(qp, kp, vp, causal=True, sm_scale=wl.SCALE_TEXT,
+                                                   num_key_value_groups=2), 10, 3, world, device), flops, "tflops")
+    del qp, kp, vp
+    qv, kv_, vv, cu, seg = wl.cfg3_varlen(seed=0, device=device)
+    vflops = sum(4 * n * n * 64 * 16 for n in seg)
+    cache: dict = {}
+    out["vit_cfg3"] = pair(
+        _time_calls(lambda: ref.varlen_flash_attention(qv, kv_, vv, cu_seq_lens_q=cu, cu_seq_lens_k=cu,
+                                                       sm_scale=wl.SCALE_VIT, max_length_q=max(seg),
+                                                       max_length_k=max(seg), metadata_cache=cache), 10, 3, world, device),
+        _time_calls(lambda: ab.varlen_flash_attention(qv, kv_, vv, cu_seq_lens_q=cu, cu_seq_lens_k=cu,
+                                                      sm_scale=wl.SCALE_VIT), 10, 3, world, device), vflops, "tflops")
+    del qv, kv_, vv
+
+    # ---- the native fp16 decode kernel (dujunbaoV1/native_cuda_ops), at the shapes it takes
+    if (REF_DIR / "native_cuda_ops").exists():
+        try:
+            nat_ops = _load_ref_package("native_cuda_ops", "ref_native_cuda_ops")
+            avail = nat_ops.is_available()
+        except Exception as exc:  # noqa: BLE001
+            avail, nat_ops = False, None
+            out["native_decode_q1_gqa"] = {"unavailable": f"import failed: {exc}"}
+        if avail:
+            g = wl.generator(4, device)
+            qn = wl.randn((B, 16, 1, 128), g, torch.float16, device)
+            kn = wl.randn((B, 8, 1024, 128), g, torch.float16, device)
+            vn = wl.randn((B, 8, 1024, 128), g, torch.float16, device)
+            q3 = qn[:, :, 0].contiguous()
+            nb = 2 * B * 8 * 1024 * 128 * 2 + 2 * B * 16 * 128 * 2
+            out["native_decode_q1_gqa"] = {
+                **pair(_time_calls(lambda: nat_ops.decode_q1_gqa_forward(q3, kn, vn, 1024, wl.SCALE_TEXT), 10, 3, world,
+                                   device),
+                       _time_calls(lambda: ab.gqa_decode_attention(qn, kn, vn, sm_scale=wl.SCALE_TEXT,
+                                                                   num_key_value_groups=2), 20, 3, world, device),
+                       nb, "gbs"),
+                "shape": "B64 Hq16 Hkv8 L1024 D128 fp16 (its head_dim and cache-length limits)"}
+        elif "native_decode_q1_gqa" not in out:
+            out["native_decode_q1_gqa"] = {"unavailable": f"extension did not load: {nat_ops.IMPORT_ERROR}"}
+    else:
+        out["native_decode_q1_gqa"] = {"unavailable": "not built in baseline/_ref"}
+    torch.cuda.empty_cache()
+    return out
+
+
 # ------------------------------------------------------------------ CPU (reference) path
 
 
@@ -866,13 +1054,20 @@ def _main(out: "_JsonStdout", argv=None) -> int:
     ap.add_argument("--no-secondary", dest="secondary", action="store_false",
                     help="skip the tensor-core prefill / ViT measurements")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    ap.add_argument("--no-refgpu", dest="refgpu", action="store_false",
+                    help="skip timing the reference's own GPU kernels beside ours (N=1 only)")
     ap.add_argument("--no-e2e", dest="e2e", action="store_false", help="skip the end-to-end host-buffer measurement")
     ap.add_argument("--no-generate", dest="generate", action="store_false",
                     help="skip the end-to-end greedy generate on the random-init Qwen3-VL-2B-shaped model")
-    ap.add_argument("--only", choices=["decode", "split_kv", "prefill", "vit", "products", "generate"], default=None,
-                    help="run one workload (profiling)")
+    ap.add_argument("--only", choices=["decode", "split_kv", "prefill", "vit", "products", "generate", "refgpu"],
+                    default=None, help="run one workload (profiling; refgpu: the reference's own GPU kernels beside ours)")
+    ap.add_argument("--install-reference", type=Path, default=None, metavar="SRC",
+                    help="install the reference checkout at SRC under baseline/_ref for --only refgpu, then exit")
     ap.add_argument("--layers", type=int, default=LAYERS, help="decode layers per step (28 = Qwen3-VL-2B)")
     args = ap.parse_args(argv)
+    if args.install_reference is not None:
+        out.emit({"install_reference": install_reference(args.install_reference.resolve())})
+        return 0
     if args.warmup < 3:
         args.warmup = 3
     world, rank, local = dist_info()
@@ -907,6 +1102,8 @@ def _main(out: "_JsonStdout", argv=None) -> int:
         result.update(run_fmha_secondary(args, world, device, peaks, only))
     if args.secondary and only in (None, "products"):
         result["decode_products"] = run_products(args, world, device, peaks)
+    if only == "refgpu" or (only is None and world == 1 and args.refgpu):
+        result["reference_gpu"] = run_refgpu(args, world, device, peaks)
     if world == 1 and ((args.generate and only is None) or only == "generate"):
         result["generate_cfg4"] = run_generate(device)
     line = None
