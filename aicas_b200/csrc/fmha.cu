@@ -599,7 +599,9 @@ __global__ void __launch_bounds__(threads_for<KT>(), 3 - KT) fmha_fwd_kernel(con
       // ex2.approx; partial sums in f32x2 accumulators.
       uint64_t rs2[2] = {f2(0.f, 0.f), f2(0.f, 0.f)};
       const uint64_t c2 = f2(c, c), nm2 = f2(-m_use, -m_use);
-      uint32_t pk[kBN / 2];
+      // the packed pair e overwrites v[e]: v[2e] and v[2e + 1] are read first,
+      // and no later pair reads below index 2e + 2, so P takes no registers of its own
+      uint32_t* pk = v;
       if (mask) {
 #pragma unroll
         for (int e = 0; e < kBN / 2; ++e) {
