@@ -19,8 +19,18 @@ preallocated cache and the decode step replayed from one CUDA graph, driven by
 the fused RoPE + append kernel), the serving path a deployment would use.
 
 What is compared (the tolerances live in the tests that call these helpers):
+  * ``forced_agreement``: at every position of SDPA's own greedy sequence, fed
+    SDPA's tokens (teacher forcing through ``generate``, so prefill and every
+    decode step run on this backend), the fraction of positions where this
+    backend's greedy choice is SDPA's.  Free-running sequences of a random-init
+    model part after the first near-tie and then have nothing in common, even
+    between two correct attentions; this metric does not compound.  With
+    ``with_control`` the same is measured for SDPA with its softmax scale off
+    by 10% (``control_forced_agreement``), a wrong attention of the size a
+    kernel bug makes, to show what a failing value looks like;
   * ``token_match``: the fraction of generated positions where the patched and
-    the SDPA greedy sequences agree, counted up to their first divergence;
+    the SDPA greedy sequences agree, counted up to their first divergence
+    (informational: see above);
   * ``max_logit_gap``: the patched tokens fed back, teacher-forced, through
     the SDPA model: at every generated position, SDPA's best logit minus its
     logit for the patched token (0 where SDPA would pick the same token).  On
@@ -213,6 +223,62 @@ def greedy_generate(model, inputs: dict, max_new_tokens: int, timed: bool = True
     return GenerateRun(tokens=out[:, inputs["input_ids"].shape[1]:], seconds=dt, ttft_seconds=ttft)
 
 
+class _ForceAndRecord:
+    """Logits processor for ``generate``: records the model's own greedy choice
+    at each step, then forces ``forced[:, step]``, so every step sees the same
+    prefix as the run that produced ``forced``."""
+
+    def __init__(self, forced: torch.Tensor):
+        self.forced = forced
+        self.choices: list[torch.Tensor] = []
+
+    def __call__(self, input_ids: torch.Tensor, scores: torch.Tensor) -> torch.Tensor:
+        step = len(self.choices)
+        self.choices.append(scores.argmax(dim=-1))
+        out = torch.full_like(scores, float("-inf"))
+        out.scatter_(1, self.forced[:, step:step + 1].to(scores.device), 0.0)
+        return out
+
+
+@torch.no_grad()
+def forced_choices(model, inputs: dict, forced: torch.Tensor) -> torch.Tensor:
+    """[B, n] the model's greedy choice at each of ``forced``'s n positions when
+    ``forced`` is fed back as the continuation (prefill, then n - 1 decode steps
+    on the KV cache, through ``generate``)."""
+    from transformers import LogitsProcessorList
+
+    proc = _ForceAndRecord(forced)
+    model.generate(**inputs, max_new_tokens=forced.shape[1], min_new_tokens=forced.shape[1], do_sample=False,
+                   use_cache=True, pad_token_id=0, logits_processor=LogitsProcessorList([proc]))
+    return torch.stack(proc.choices, dim=1)
+
+
+def _perturbed_sdpa(module, query, key, value, attention_mask, dropout=0.0, scaling=None, **kwargs):
+    """SDPA with the softmax scale off by 10%: a wrong attention of the kind a
+    kernel bug would produce, for the control of the agreement metric."""
+    from transformers.integrations.sdpa_attention import sdpa_attention_forward
+
+    s = module.scaling if scaling is None else scaling
+    return sdpa_attention_forward(module, query, key, value, attention_mask, dropout=dropout, scaling=1.1 * s, **kwargs)
+
+
+PERTURBED_KEY = "aicas_control_sdpa_scale_1p1"
+
+
+def set_text_attention_control(model) -> None:
+    """The language model on :func:`_perturbed_sdpa` (vision stays on SDPA)."""
+    from transformers.masking_utils import ALL_MASK_ATTENTION_FUNCTIONS
+    from transformers.modeling_utils import ALL_ATTENTION_FUNCTIONS
+
+    if PERTURBED_KEY not in ALL_ATTENTION_FUNCTIONS:
+        ALL_ATTENTION_FUNCTIONS.register(PERTURBED_KEY, _perturbed_sdpa)
+    if PERTURBED_KEY not in ALL_MASK_ATTENTION_FUNCTIONS:
+        ALL_MASK_ATTENTION_FUNCTIONS.register(PERTURBED_KEY, ALL_MASK_ATTENTION_FUNCTIONS["sdpa"])
+    set_attention(model, "sdpa")
+    model.config.text_config._attn_implementation = PERTURBED_KEY
+    model.model.language_model.config._attn_implementation = PERTURBED_KEY
+
+
 def token_match(a: torch.Tensor, b: torch.Tensor) -> float:
     """Fraction of positions (over the batch) before each row's first
     disagreement."""
@@ -265,7 +331,8 @@ def teacher_forced_gap(model, inputs: dict, tokens: torch.Tensor) -> torch.Tenso
 
 def run_check(batch: int = 8, seq_len: int = 2048, max_new_tokens: int = 128, grid_hw=(64, 100),
               dtype: torch.dtype = torch.bfloat16, device: str | torch.device = "cuda:0", seed: int = 0,
-              text: dict | None = None, vision: dict | None = None, timed: bool = True) -> dict:
+              text: dict | None = None, vision: dict | None = None, timed: bool = True,
+              with_control: bool = False) -> dict:
     """Build the model, generate greedily with SDPA and with this backend, and
     compare.  Returns the numbers the integration test and the benchmark
     report."""
@@ -283,6 +350,13 @@ def run_check(batch: int = 8, seq_len: int = 2048, max_new_tokens: int = 128, gr
     ours = greedy_generate(model, inputs, max_new_tokens, timed)
     graph_generate(model, warm, 3, timed=False)
     graph = graph_generate(model, inputs, max_new_tokens, timed)
+    # position-wise agreement: this backend's greedy choice at every position of
+    # SDPA's own greedy sequence, fed SDPA's tokens (no compounding after a near-tie)
+    agree = float((forced_choices(model, inputs, ref.tokens) == ref.tokens).float().mean())
+    control = None
+    if with_control:
+        set_text_attention_control(model)
+        control = float((forced_choices(model, inputs, ref.tokens) == ref.tokens).float().mean())
     set_attention(model, "sdpa")
     gap = teacher_forced_gap(model, inputs, ours.tokens)
     gap_graph = teacher_forced_gap(model, inputs, graph.tokens)
@@ -293,6 +367,8 @@ def run_check(batch: int = 8, seq_len: int = 2048, max_new_tokens: int = 128, gr
         "image_grid": list(grid_hw),
         "dtype": str(dtype).replace("torch.", ""),
         "token_match": token_match(ours.tokens, ref.tokens),
+        "forced_agreement": agree,
+        "control_forced_agreement": control,
         "max_logit_gap": float(gap.max()),
         "mean_logit_gap": float(gap.mean()),
         "patched": {"tokens_per_s": ours.tokens_per_s, "seconds": ours.seconds, "ttft_s": ours.ttft_seconds},

@@ -929,7 +929,8 @@ def run_generate(device) -> dict:
     timed around device-synchronised generate calls; not a roofline)."""
     from aicas_b200 import integration
 
-    r = integration.run_check(batch=8, seq_len=2048, max_new_tokens=128, grid_hw=(64, 100), device=device)
+    r = integration.run_check(batch=8, seq_len=2048, max_new_tokens=128, grid_hw=(64, 100), device=device,
+                              with_control=True)
     r["workload"] = "cfg4-e2e: random-init Qwen3-VL-2B-shaped model, 8 prompts x 2048 tokens (1600 image), greedy 128"
     r["speedup_vs_sdpa"] = r["patched"]["tokens_per_s"] / r["sdpa"]["tokens_per_s"]
     torch.cuda.empty_cache()

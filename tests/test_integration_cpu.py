@@ -61,6 +61,27 @@ def test_greedy_generate_and_teacher_forced_gap(tiny):
     assert float(it.teacher_forced_gap(model, inp, other)[:, 0].min()) > 0
 
 
+def test_forced_choices_reproduce_the_greedy_run_and_see_a_wrong_attention(tiny):
+    """Fed its own greedy tokens, the same model picks them at every position;
+    a continuation that is not its own is followed all the same (each step sees
+    the forced prefix), and the perturbed-attention control disagrees somewhere."""
+    cfg, model = tiny
+    inp = it.synthetic_prompt(cfg, batch=2, seq_len=48, grid_hw=(4, 6), text_before=8)
+    it.set_attention(model, "sdpa")
+    run = it.greedy_generate(model, inp, 6, timed=False)
+    assert torch.equal(it.forced_choices(model, inp, run.tokens), run.tokens)
+    other = torch.randint(0, 1000, run.tokens.shape)
+    choices = it.forced_choices(model, inp, other)
+    assert choices.shape == other.shape and torch.equal(choices[:, 0], run.tokens[:, 0])
+    it.set_text_attention_control(model)
+    try:
+        assert it.attention_in_use(model)[1] == it.PERTURBED_KEY
+        ctrl = it.forced_choices(model, inp, run.tokens)
+        assert ctrl.shape == run.tokens.shape
+    finally:
+        it.set_attention(model, "sdpa")
+
+
 def test_token_match_counts_up_to_the_first_divergence():
     a = torch.tensor([[1, 2, 3, 4], [5, 6, 7, 8]])
     b = torch.tensor([[1, 2, 0, 4], [5, 6, 7, 8]])
