@@ -35,6 +35,7 @@ CAP_ROPE_APPEND = 16
 CAP_PEER_EXCHANGE = 32
 CAP_DECODE_LINEAR = 64
 CAP_VISION_ROPE = 128
+CAP_VISION_QKV = 256
 
 LINEAR_MAX_SEGMENTS = 4
 LINEAR_MAX_ROWS = 32
@@ -125,6 +126,14 @@ class VisionRopeParams(ctypes.Structure):
     ]
 
 
+class VisionQkvParams(ctypes.Structure):
+    _fields_ = [
+        ("x", _vp), ("x_stride", _i64), ("weight", _vp), ("weight_stride", _i64), ("bias", _vp),
+        ("cos", _vp), ("sin", _vp), ("cs_stride_t", _i64), ("out", _vp), ("out_stride", _i64),
+        ("tokens", _i32), ("in_features", _i32), ("heads", _i32), ("head_dim", _i32), ("dtype", _i32),
+    ]
+
+
 class LinearSegment(ctypes.Structure):
     _fields_ = [("weight", _vp), ("weight_stride", _i64), ("out", _vp), ("out_stride", _i64), ("rows", _i32)]
 
@@ -156,6 +165,7 @@ EXPORTS = {
     "aicas_varlen_attention": (ctypes.c_int, [ctypes.POINTER(FmhaParams), _vp]),
     "aicas_rope_kv_append": (ctypes.c_int, [ctypes.POINTER(RopeAppendParams), _vp]),
     "aicas_vision_rope": (ctypes.c_int, [ctypes.POINTER(VisionRopeParams), _vp]),
+    "aicas_vision_qkv_rope": (ctypes.c_int, [ctypes.POINTER(VisionQkvParams), _vp]),
     "aicas_linear_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(LinearParams)]),
     "aicas_decode_linear": (ctypes.c_int, [ctypes.POINTER(LinearParams), _vp, ctypes.c_size_t, _vp]),
     "aicas_version": (ctypes.c_char_p, []),

@@ -12,6 +12,7 @@
 #include "common.cuh"
 #include "fmha.cuh"
 #include "linear.cuh"
+#include "vision_qkv.cuh"
 
 namespace aicas {
 
@@ -386,7 +387,7 @@ const char* aicas_version(void) { return "aicas_b200 0.2.0 sm_100a abi 2"; }
 
 uint32_t aicas_capabilities(void) {
   return AICAS_CAP_DECODE | AICAS_CAP_MERGE | AICAS_CAP_ROPE_APPEND | AICAS_CAP_PEER_EXCHANGE |
-         AICAS_CAP_DECODE_LINEAR | AICAS_CAP_VISION_ROPE | aicas::fmha_capabilities();
+         AICAS_CAP_DECODE_LINEAR | AICAS_CAP_VISION_ROPE | AICAS_CAP_VISION_QKV | aicas::fmha_capabilities();
 }
 
 const char* aicas_last_error(void) { return g_err; }
@@ -671,6 +672,35 @@ int aicas_vision_rope(const aicas_vision_rope_params* p, void* stream) {
   const cudaError_t e = aicas::launch_vision_rope(p->dtype, a, sm_count(), static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "vision RoPE launch");
   return AICAS_OK;
+}
+
+int aicas_vision_qkv_rope(const aicas_vision_qkv_params* p, void* stream) {
+  if (p == nullptr) return fail(AICAS_ERR_INVALID, "params is NULL");
+  if (p->dtype != AICAS_DTYPE_F16 && p->dtype != AICAS_DTYPE_BF16)
+    return fail(AICAS_ERR_UNSUPPORTED, "vision QKV needs fp16 or bf16 (dtype %d)", p->dtype);
+  if (p->tokens < 0 || p->heads <= 0 || p->in_features <= 0)
+    return fail(AICAS_ERR_INVALID, "tokens=%d heads=%d in_features=%d", p->tokens, p->heads, p->in_features);
+  if (p->head_dim != 64 || p->heads % 4 != 0)
+    return fail(AICAS_ERR_UNSUPPORTED, "vision QKV needs head_dim 64 and a multiple of 4 heads (got %d, %d)",
+                p->head_dim, p->heads);
+  if (p->in_features % 64 != 0)
+    return fail(AICAS_ERR_UNSUPPORTED, "vision QKV needs in_features a multiple of 64 (got %d)", p->in_features);
+  if (p->tokens == 0) return AICAS_OK;
+  const int64_t n = 3LL * p->heads * p->head_dim;
+  if (p->x == nullptr || p->weight == nullptr || p->out == nullptr || p->cos == nullptr || p->sin == nullptr)
+    return fail(AICAS_ERR_INVALID, "x, weight, out, cos and sin must be set");
+  if (!aligned16(p->x) || !aligned16(p->weight) || !aligned16(p->out) || !aligned16(p->cos) || !aligned16(p->sin))
+    return fail(AICAS_ERR_INVALID, "device pointers must be 16-byte aligned");
+  if (p->bias != nullptr && !aligned16(p->bias)) return fail(AICAS_ERR_INVALID, "bias must be 16-byte aligned");
+  if (p->x_stride < p->in_features || !stride_ok(p->x_stride, 2) || p->weight_stride < p->in_features ||
+      !stride_ok(p->weight_stride, 2))
+    return fail(AICAS_ERR_INVALID, "x/weight strides must be >= in_features and multiples of 8 elements");
+  if (p->out_stride < n || !stride_ok(p->out_stride, 2))
+    return fail(AICAS_ERR_INVALID, "out_stride must be >= 3 * heads * head_dim and a multiple of 8");
+  if (p->cs_stride_t < p->head_dim || (p->cs_stride_t & 3) != 0)
+    return fail(AICAS_ERR_INVALID, "cos/sin row stride must be >= head_dim and a multiple of 4");
+  return aicas::run_vision_qkv(p, sm_count(), static_cast<cudaStream_t>(stream), device_error_word(), g_err,
+                               sizeof(g_err));
 }
 
 size_t aicas_linear_workspace_bytes(const aicas_linear_params* p) {

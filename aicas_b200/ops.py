@@ -709,3 +709,55 @@ def vision_rope(query: torch.Tensor, key: torch.Tensor, cos: torch.Tensor, sin: 
 
     _call_in_device(query.device, run)
     return q_out, k_out
+
+
+# ---------------------------------------------------------------------- vision QKV projection + RoPE
+
+
+def vision_qkv_rope(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None, cos: torch.Tensor,
+                    sin: torch.Tensor, num_heads: int) -> torch.Tensor:
+    """The vision attention's packed projection and RoPE in one kernel:
+    ``qkv = x W^T + b`` (``nn.Linear``, transformers
+    models/qwen3_vl/modeling_qwen3_vl.py:205) viewed ``[T, 3, H, D]``, with
+    ``apply_rotary_pos_emb_vision`` (:131-142) applied to its q and k parts.
+
+    x ``[T, K]``, weight ``[3*H*D, K]``, bias ``[3*H*D]`` or None (fp16/bf16,
+    one dtype), cos/sin ``[T, D]`` (used as fp32).  Returns a new ``[T, 3, H, D]``
+    tensor; ``[:, 0]``, ``[:, 1]``, ``[:, 2]`` are the rotated q, the rotated k
+    and v.  Needs D == 64, H a multiple of 4, K a multiple of 64."""
+    tensors = [x, weight] + ([bias] if bias is not None else [])
+    _reject_grad(*tensors)
+    if not all(t.is_cuda for t in tensors + [cos, sin]):
+        raise ValueError("vision_qkv_rope needs CUDA tensors")
+    if x.dtype not in _LINEAR_DTYPES or any(t.dtype != x.dtype for t in tensors):
+        raise ValueError("vision_qkv_rope needs fp16 or bf16 x, weight and bias of one dtype")
+    x = _row_major(x, "x")
+    weight = _row_major(weight, "weight")
+    T, K = x.shape
+    N = weight.shape[0]
+    if weight.shape[1] != K or N % (3 * num_heads) != 0:
+        raise ValueError(f"weight must be [3 * heads * head_dim, {K}]")
+    D = N // (3 * num_heads)
+    if bias is not None:
+        if bias.shape != (N,):
+            raise ValueError(f"bias must be a [{N}] tensor")
+        if not bias.is_contiguous() or bias.data_ptr() % 16:
+            bias = bias.contiguous().clone()
+    if cos.shape != (T, D) or sin.shape != (T, D):
+        raise ValueError(f"cos/sin must be [{T}, {D}]")
+    cos, sin = cos.float().contiguous(), sin.float().contiguous()
+    out = torch.empty((T, 3, num_heads, D), dtype=x.dtype, device=x.device)
+    if T == 0:
+        return out
+    p = nat.VisionQkvParams()
+    p.x, p.x_stride, p.weight, p.weight_stride = x.data_ptr(), x.stride(0), weight.data_ptr(), weight.stride(0)
+    p.bias = _ptr(bias)
+    p.cos, p.sin, p.cs_stride_t = cos.data_ptr(), sin.data_ptr(), cos.stride(0)
+    p.out, p.out_stride = out.data_ptr(), out.stride(0)
+    p.tokens, p.in_features, p.heads, p.head_dim, p.dtype = T, K, num_heads, D, _LINEAR_DTYPES[x.dtype]
+
+    def run():
+        nat.check(nat.lib().aicas_vision_qkv_rope(ctypes.byref(p), _stream_handle(x.device)), "aicas_vision_qkv_rope")
+
+    _call_in_device(x.device, run)
+    return out

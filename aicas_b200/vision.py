@@ -6,8 +6,10 @@ packed linear, splits q/k/v, rotates q and k with
 ``apply_rotary_pos_emb_vision`` -- fp32 copies and about eight elementwise
 kernels per tensor -- and hands the three to the attention interface.
 :func:`fused_vision_attention_forward` is the same computation with the
-rotation in one kernel (:func:`aicas_b200.ops.vision_rope`, bit-identical);
-the packed projection stays a library GEMM and v stays a view of it.
+projection, its bias, the split and the rotation in one tensor-core kernel
+(:func:`aicas_b200.ops.vision_qkv_rope`); projections that kernel does not
+take (other head sizes) keep the library GEMM followed by the one-kernel
+rotation (:func:`aicas_b200.ops.vision_rope`, bit-identical to HF).
 :func:`install_vision_rope_fusion` puts it on every vision attention module of
 a model.
 """
@@ -28,9 +30,14 @@ def fused_vision_attention_forward(self, hidden_states: torch.Tensor, cu_seqlens
     from transformers.models.qwen3_vl.modeling_qwen3_vl import eager_attention_forward
 
     seq_length = hidden_states.shape[0]
-    qkv = self.qkv(hidden_states).view(seq_length, 3, self.num_heads, -1)
     cos, sin = position_embeddings
-    query_states, key_states = ops.vision_rope(qkv[:, 0], qkv[:, 1], cos, sin)
+    if _projection_fusable(self, hidden_states):
+        # projection, bias, split and RoPE in one tensor-core kernel
+        qkv = ops.vision_qkv_rope(hidden_states, self.qkv.weight, self.qkv.bias, cos, sin, self.num_heads)
+        query_states, key_states = qkv[:, 0], qkv[:, 1]
+    else:
+        qkv = self.qkv(hidden_states).view(seq_length, 3, self.num_heads, -1)
+        query_states, key_states = ops.vision_rope(qkv[:, 0], qkv[:, 1], cos, sin)
     query_states = query_states.transpose(0, 1).unsqueeze(0)
     key_states = key_states.transpose(0, 1).unsqueeze(0)
     value_states = qkv[:, 2].transpose(0, 1).unsqueeze(0)
@@ -43,6 +50,19 @@ def fused_vision_attention_forward(self, hidden_states: torch.Tensor, cu_seqlens
                                          max_length_k=max_seqlen, is_causal=False, **kwargs)
     attn_output = attn_output.reshape(seq_length, -1).contiguous()
     return self.proj(attn_output)
+
+
+def _projection_fusable(module, hidden_states: torch.Tensor) -> bool:
+    """Whether ``aicas_vision_qkv_rope`` takes this module's projection: a plain
+    ``nn.Linear`` of the hidden states' 16-bit dtype, head_dim 64, a multiple
+    of 4 heads and of 64 input features (Qwen3-VL-2B's vision tower: 16 heads
+    of 64 over 1024 features)."""
+    lin = module.qkv
+    if type(lin) is not torch.nn.Linear or hidden_states.ndim != 2:
+        return False
+    heads, (n, k) = module.num_heads, lin.weight.shape
+    return (hidden_states.dtype in (torch.float16, torch.bfloat16) and lin.weight.dtype == hidden_states.dtype
+            and n == 3 * heads * 64 and heads % 4 == 0 and k % 64 == 0)
 
 
 def install_vision_rope_fusion(model) -> int:

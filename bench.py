@@ -608,7 +608,55 @@ def run_fmha_secondary(args, world, device, peaks, only=None) -> dict:
         else:
             out["vit_cfg3"] = time_varlen(args, world, device, peaks)
         out["vision_rope_cfg3"] = time_vision_rope(args, world, device, peaks)
+        if caps & _native.CAP_VISION_QKV:
+            out["vision_qkv_cfg3"] = time_vision_qkv(args, world, device, peaks)
     return out
+
+
+def time_vision_qkv(args, world, device, peaks) -> dict:
+    """The vision attention's packed projection + split + RoPE at config 3's
+    token count (hidden 1024, 16 heads of 64): one tensor-core kernel
+    (aicas_vision_qkv_rope) against HF's path on the same tensors (nn.Linear
+    through cuBLAS, then apply_rotary_pos_emb_vision) and against cuBLAS
+    followed by the one-kernel RoPE."""
+    from transformers.models.qwen3_vl.modeling_qwen3_vl import apply_rotary_pos_emb_vision
+
+    from aicas_b200 import ops
+    from aicas_b200 import workloads as wl
+
+    _, _, _, cu, _ = wl.cfg3_varlen(seed=0, device=device)
+    T, K, H = int(cu[-1]), 1024, 16
+    g = torch.Generator(device=device).manual_seed(0)
+    x = torch.randn(T, K, device=device, generator=g).to(torch.bfloat16)
+    w = (torch.randn(3 * H * 64, K, device=device, generator=g) / K ** 0.5).to(torch.bfloat16)
+    b = (0.1 * torch.randn(3 * H * 64, device=device, generator=g)).to(torch.bfloat16)
+    emb = torch.randn(T, 32, device=device, generator=g).repeat(1, 2)
+    cos, sin = emb.cos(), emb.sin()
+
+    def hf():
+        qkv = torch.nn.functional.linear(x, w, b).view(T, 3, H, 64)
+        return apply_rotary_pos_emb_vision(qkv[:, 0], qkv[:, 1], cos, sin)
+
+    def cublas_then_rope():
+        qkv = torch.nn.functional.linear(x, w, b).view(T, 3, H, 64)
+        return ops.vision_rope(qkv[:, 0], qkv[:, 1], cos, sin)
+
+    st = {}
+    ms = _time_calls(lambda: ops.vision_qkv_rope(x, w, b, cos, sin, H), 20, 3, world, device, st)
+    gemm_ms = _time_calls(lambda: torch.nn.functional.linear(x, w, b), 20, 3, world, device)
+    hf_ms = _time_calls(hf, 10, 3, world, device)
+    split_ms = _time_calls(cublas_then_rope, 10, 3, world, device)
+    flops = 2 * T * 3 * H * 64 * K
+    tf = flops / (ms * 1e-3) / 1e12
+    return {"value": round(world * tf, 1), "unit": "TFLOP/s", "ms_per_call": round(ms, 4),
+            "median_ms_per_call": round(st["median_ms"], 4), "per_gpu_tflops": round(tf, 1),
+            "frac_of_bf16_peak": round(tf / peaks["bf16_tflops"], 4), "flops_per_call": flops,
+            "cublas_linear_alone_ms": round(gemm_ms, 4),
+            "cublas_linear_tflops": round(flops / (gemm_ms * 1e-3) / 1e12, 1),
+            "hf_path_ms": round(hf_ms, 4), "cublas_then_fused_rope_ms": round(split_ms, 4),
+            "speedup_vs_hf_path": round(hf_ms / ms, 2),
+            "config": f"T={T} patches, x [T, 1024] bf16, W [3072, 1024], bias, 16 heads of 64, fp32 cos/sin",
+            "scaling": "weak (replicas)"}
 
 
 def time_vision_rope(args, world, device, peaks) -> dict:

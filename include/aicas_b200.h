@@ -39,6 +39,10 @@
  *                             models/qwen3_vl/modeling_qwen3_vl.py:131-142) as the
  *                             vision attention applies it after splitting the
  *                             packed QKV projection (:205-209), in one kernel
+ *   aicas_vision_qkv_rope     the vision attention's packed QKV projection (nn.Linear,
+ *                             transformers models/qwen3_vl/modeling_qwen3_vl.py:205)
+ *                             with the split and apply_rotary_pos_emb_vision (:206-209,
+ *                             :131-142) in its epilogue, one kernel
  *   aicas_decode_linear       the decode-side matrix-vector products of
  *                             dujunbaoV1/native_cuda_ops/decode_q1_gqa_kernel.cu:
  *                             rmsnorm_kernel :127-157 (as a fused prologue),
@@ -292,6 +296,31 @@ typedef struct aicas_vision_rope_params {
 AICAS_API int aicas_vision_rope(const aicas_vision_rope_params* p, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* Vision-tower packed QKV projection with the RoPE of q and k in its        */
+/* epilogue, on the tensor cores: out = [q_rot | k_rot | v] of x W^T + b.    */
+/* ------------------------------------------------------------------------ */
+typedef struct aicas_vision_qkv_params {
+  const void* x;            /* [T, K] patch features, x_stride elements between rows */
+  int64_t x_stride;
+  const void* weight;       /* [3 * H * D, K] (nn.Linear layout), weight_stride elements between rows */
+  int64_t weight_stride;
+  const void* bias;         /* optional [3 * H * D], 16-byte aligned */
+  const float* cos;         /* [T, D] fp32 */
+  const float* sin;         /* [T, D] fp32 */
+  int64_t cs_stride_t;      /* row stride of cos and sin (a multiple of 4) */
+  void* out;                /* [T, 3, H, D]: out_stride elements between token rows (>= 3 * H * D);
+                               the x W^T + b of q and k rotated as HF rotates them, v as projected */
+  int64_t out_stride;
+  int32_t tokens;           /* T (0: nothing to do) */
+  int32_t in_features;      /* K, a positive multiple of 64 */
+  int32_t heads;            /* H, a multiple of 4 */
+  int32_t head_dim;         /* D, 64 */
+  int32_t dtype;            /* AICAS_DTYPE_F16 or AICAS_DTYPE_BF16, shared by x, weight, bias, out */
+} aicas_vision_qkv_params;
+
+AICAS_API int aicas_vision_qkv_rope(const aicas_vision_qkv_params* p, void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* Decode-side weight-streaming products: Y = epilogue(X' W^T) for a few rows */
 /* X (the batch of one decode step) on the tensor cores.                      */
 /* ------------------------------------------------------------------------ */
@@ -357,6 +386,7 @@ AICAS_API const char* aicas_version(void);
 #define AICAS_CAP_PEER_EXCHANGE 32u
 #define AICAS_CAP_DECODE_LINEAR 64u
 #define AICAS_CAP_VISION_ROPE 128u
+#define AICAS_CAP_VISION_QKV 256u
 AICAS_API uint32_t aicas_capabilities(void);
 
 /* Message of the last failed call on this thread ("" if none). */
