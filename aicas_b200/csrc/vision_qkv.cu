@@ -13,13 +13,15 @@
 //
 // Persistent, one CTA per SM, warp-specialised:
 //   warp 0      TMA producer: x tile 128 x 64 and W tile 256 x 64 per K step
-//               (128-byte swizzle) into a 4-stage ring
+//               (128-byte swizzle) into a 3-stage ring
 //   warp 1      TMEM allocator and the single MMA-issuing thread: tcgen05.mma
 //               M=128 N=256 K=16, accumulating a 128 x 256 output tile in one of
 //               two TMEM buffers (2 x 256 columns)
 //   warps 4-11  epilogue (two warpgroups, half of every head's columns
 //               each), one output row (TMEM lane) per thread, reading one
-//               buffer while the tensor core fills the other
+//               buffer while the tensor core fills the other; the finished
+//               tile is staged in shared memory and written by TMA stores
+//               (whole lines, rows past T clipped by the tensor map)
 // Tiles go out m-block-major (12 column tiles of one 128-row block one after
 // another), so the CTAs working at the same time share their x rows in L2; W
 // (6 MB at Qwen3-VL-2B's size) stays in L2.
@@ -38,11 +40,15 @@ namespace {
 constexpr int kQBM = 128;     // token rows per tile
 constexpr int kQBN = 256;     // output features per tile (four 64-wide heads)
 constexpr int kQBK = 64;      // K per stage (128 bytes of bf16: one swizzle row)
-constexpr int kQStages = 4;
+constexpr int kQStages = 3;
 constexpr uint32_t kQATile = kQBM * kQBK * 2;   // 16 KB
 constexpr uint32_t kQBTile = kQBN * kQBK * 2;   // 32 KB
 constexpr uint32_t kQStage = kQATile + kQBTile;  // 48 KB
-constexpr uint32_t kQBarOff = kQStages * kQStage;
+// the output tile staged for the TMA store: four [128 rows x 64 columns]
+// boxes (one per head), 128-byte swizzled rows
+constexpr uint32_t kQOutOff = kQStages * kQStage;
+constexpr uint32_t kQOutBox = kQBM * 64 * 2;     // 16 KB
+constexpr uint32_t kQBarOff = kQOutOff + 4 * kQOutBox;
 constexpr int kQNumBars = 2 * kQStages + 4 + 1;  // full, empty, acc_full[2], acc_empty[2], mma_done
 constexpr uint32_t kQMisc = kQBarOff + kQNumBars * 8;
 constexpr uint32_t kQSmem = kQMisc + 64 + 1024;  // + slack to align the base to 1024
@@ -51,12 +57,11 @@ constexpr int kQThreads = 384;  // producer, MMA, 2 idle warps, two epilogue war
 struct VisionQkvArgs {
   CUtensorMap tm_x;  // [T, K], box {64, 128}
   CUtensorMap tm_w;  // [N, K], box {64, 256}
+  CUtensorMap tm_o;  // [T, N], box {64, 128}: the store of one head's 64 columns of a tile
   const void* bias;  // [N] or null
   const float* cos;  // [T, D]
   const float* sin;
   int64_t cs_st;
-  void* out;         // [T, N] row stride out_st
-  int64_t out_st;
   int tokens, k_steps, n_tiles, m_tiles, rope_cols;  // rope_cols: the first 2*H*D columns are q and k
   unsigned int* err;
 };
@@ -75,6 +80,18 @@ __device__ __forceinline__ uint32_t pack_pair(float lo, float hi) {
 template <typename T>
 __device__ __forceinline__ float round_to(float x) {
   return Elem<T>::to_float(Elem<T>::from_float(x));
+}
+
+// Named barrier 1 over the two epilogue warpgroups (256 threads), returning
+// the OR of their predicates so that all of them take the same branch after it.
+__device__ __forceinline__ bool epilogue_any(bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, 256, p;\n selp.u32 %0, 1, 0, q;\n}"
+      : "=r"(r)
+      : "r"((uint32_t)pred)
+      : "memory");
+  return r != 0;
 }
 
 template <typename T>
@@ -214,10 +231,17 @@ __global__ void __launch_bounds__(kQThreads, 1) vision_qkv_kernel(const __grid_c
     const T* bias = static_cast<const T*>(a.bias);
     int it = 0;
     bool ok = !*abort_flag;
+    const bool issuer = threadIdx.x == 128;  // issues the tile's TMA stores
+    uint8_t* stage_row = gb + kQOutOff + r * 128;
     for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x, ++it) {
       const int buf = it & 1, use = it >> 1;
       const int m0 = (tile / a.n_tiles) * kQBM, n0 = (tile % a.n_tiles) * kQBN;
-      if (!__all_sync(0xffffffffu, mbar_wait(acc_full(buf), use & 1, abort_flag, a.err))) {
+      // the previous tile's stores have read the staging buffer (the bar.sync
+      // below carries that to every epilogue thread); every epilogue thread
+      // takes the same path through these barriers
+      if (issuer) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+      const bool got = __all_sync(0xffffffffu, mbar_wait(acc_full(buf), use & 1, abort_flag, a.err));
+      if (epilogue_any(!got)) {
         ok = false;
         break;
       }
@@ -225,7 +249,6 @@ __global__ void __launch_bounds__(kQThreads, 1) vision_qkv_kernel(const __grid_c
       const int row = m0 + r;
       const bool live = row < a.tokens;
       const bool rope = n0 < a.rope_cols;
-      T* orow = static_cast<T*>(a.out) + (int64_t)row * a.out_st + n0;
       const float* cs = a.cos + (int64_t)row * a.cs_st;
       const float* sn = a.sin + (int64_t)row * a.cs_st;
 #pragma unroll 1
@@ -295,11 +318,27 @@ __global__ void __launch_bounds__(kQThreads, 1) vision_qkv_kernel(const __grid_c
               w2[e] = pack_pair<T>(y2[2 * e], y2[2 * e + 1]);
             }
           }
-          *reinterpret_cast<uint4*>(orow + c0) = make_uint4(w1[0], w1[1], w1[2], w1[3]);
-          *reinterpret_cast<uint4*>(orow + c0 + 32) = make_uint4(w2[0], w2[1], w2[2], w2[3]);
+          // 16-byte chunks q and q + 4 of this row in head hh's box, XOR-swizzled by row
+          uint8_t* box = stage_row + hh * kQOutBox;
+          *reinterpret_cast<uint4*>(box + ((q ^ (r & 7)) << 4)) = make_uint4(w1[0], w1[1], w1[2], w1[3]);
+          *reinterpret_cast<uint4*>(box + (((q + 4) ^ (r & 7)) << 4)) = make_uint4(w2[0], w2[1], w2[2], w2[3]);
         }
       }
+      // the staged tile is visible to the TMA unit, then one thread stores it
+      fence_proxy_async_smem();
+      epilogue_any(false);
+      if (issuer) {
+#pragma unroll
+        for (int h = 0; h < kQBN / 64; ++h)
+          asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                           reinterpret_cast<uint64_t>(&a.tm_o)),
+                       "r"(n0 + h * 64), "r"(m0), "r"(sb + kQOutOff + h * kQOutBox)
+                       : "memory");
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      }
     }
+    // the stores have finished reading shared memory before the CTA can retire
+    if (issuer) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   }
 
   // ---------------------------------------------------------------- teardown
@@ -358,14 +397,13 @@ int run_vision_qkv(const aicas_vision_qkv_params* p, int sms, cudaStream_t strea
   VisionQkvArgs a;
   memset(&a, 0, sizeof(a));
   if (!make_map_2d(&a.tm_x, p->x, bf16, p->in_features, p->tokens, p->x_stride, kQBM, err, errlen) ||
-      !make_map_2d(&a.tm_w, p->weight, bf16, p->in_features, n, p->weight_stride, kQBN, err, errlen))
+      !make_map_2d(&a.tm_w, p->weight, bf16, p->in_features, n, p->weight_stride, kQBN, err, errlen) ||
+      !make_map_2d(&a.tm_o, p->out, bf16, n, p->tokens, p->out_stride, kQBM, err, errlen))
     return AICAS_ERR_UNSUPPORTED;
   a.bias = p->bias;
   a.cos = p->cos;
   a.sin = p->sin;
   a.cs_st = p->cs_stride_t;
-  a.out = p->out;
-  a.out_st = p->out_stride;
   a.tokens = p->tokens;
   a.k_steps = p->in_features / kQBK;
   a.n_tiles = n / kQBN;

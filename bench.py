@@ -655,6 +655,7 @@ def time_vision_qkv(args, world, device, peaks) -> dict:
             "cublas_linear_tflops": round(flops / (gemm_ms * 1e-3) / 1e12, 1),
             "hf_path_ms": round(hf_ms, 4), "cublas_then_fused_rope_ms": round(split_ms, 4),
             "speedup_vs_hf_path": round(hf_ms / ms, 2),
+            "speedup_vs_cublas_then_fused_rope": round(split_ms / ms, 2),
             "config": f"T={T} patches, x [T, 1024] bf16, W [3072, 1024], bias, 16 heads of 64, fp32 cos/sin",
             "scaling": "weak (replicas)"}
 
