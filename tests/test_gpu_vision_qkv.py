@@ -19,6 +19,8 @@ from aicas_b200 import _native as nat
 from aicas_b200 import ops
 from tests.conftest import bf16_tolerance_check
 
+pytestmark = pytest.mark.gpu
+
 
 def close(out: torch.Tensor, ref: torch.Tensor, pre: torch.Tensor) -> None:
     """out/ref [T, 3, H, D]; pre: the unrotated projection [T, 3, H, D]."""
