@@ -87,6 +87,12 @@ class ExchangeParams(ctypes.Structure):
     ]
 
 
+class PeerGroup(ctypes.Structure):
+    _fields_ = [
+        ("peers", _vp * MAX_EXCHANGE_RANKS), ("world", _i32), ("rank", _i32), ("wait_budget_ns", ctypes.c_uint64),
+    ]
+
+
 class FmhaParams(ctypes.Structure):
     _fields_ = [
         ("q", _vp), ("k", _vp), ("v", _vp), ("out", _vp),
@@ -161,6 +167,9 @@ EXPORTS = {
     "aicas_peer_buffer_open": (ctypes.c_int, [_vp, ctypes.POINTER(_vp)]),
     "aicas_peer_buffer_close": (ctypes.c_int, [_vp]),
     "aicas_exchange_merge": (ctypes.c_int, [ctypes.POINTER(ExchangeParams), _vp]),
+    "aicas_decode_exchange_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(DecodeParams)]),
+    "aicas_decode_gqa_exchange": (ctypes.c_int, [ctypes.POINTER(DecodeParams), ctypes.POINTER(PeerGroup), _vp,
+                                                 ctypes.c_size_t, _vp]),
     "aicas_prefill_gqa_causal": (ctypes.c_int, [ctypes.POINTER(FmhaParams), _vp]),
     "aicas_varlen_attention": (ctypes.c_int, [ctypes.POINTER(FmhaParams), _vp]),
     "aicas_rope_kv_append": (ctypes.c_int, [ctypes.POINTER(RopeAppendParams), _vp]),

@@ -66,7 +66,27 @@ struct DecodeArgs {
   unsigned int* ws_sched; // [2] work-item counter, finished-CTA counter (with a workspace)
   int prefetch_first;     // 1: each CTA brings its first item's K/V range into L2 before the dependency wait
   unsigned int* err;      // device error word
+  // the cross-GPU merge fused into the decode (decode_gqa_kernel<..., true>):
+  // every rank's exchange buffer as mapped here (see exchange.cu for the layout)
+  void* xpeers[8];
+  int xworld, xrank;
+  long long xslot_floats;       // floats per (parity, source rank) slot
+  long long xslot_off;          // byte offset of the slots in a buffer
+  unsigned long long xbudget;   // bound of a wait for the peers, ns
 };
+
+// Exchange buffer layout, shared by the exchange kernel and the fused decode:
+//   [0, 256)      uint64 flags[32]: flags[src] = last epoch rank src published here
+//   [256, 264)    uint64 epoch: calls completed by the owner
+//   [264, 268)    uint32 CTAs of the current exchange-kernel call that have finished
+//   [512, slots)  uint64 pair_flags[B * H][8]: [pair][src] = last epoch rank src
+//                 published that (request, KV head) pair's partial here (fused decode)
+//   [slots, ...)  fp32 slots[2][world][slot_floats]: each source rank's (out, lse)
+//                 partial, double-buffered by epoch parity
+constexpr long long kExchangePairFlags = 512;
+AICAS_HD long long exchange_slots_offset(int batch, int heads) {
+  return (kExchangePairFlags + (long long)batch * heads * 8 * 8 + 255) / 256 * 256;
+}
 
 struct VisionRopeArgs {
   const void* q_in;
@@ -111,6 +131,7 @@ struct ExchangeArgs {
   int64_t o_sb, o_sh;
   int world, rank, batch, heads, hd;
   int slot_floats;
+  long long slot_off;              // byte offset of the slots in a buffer
   unsigned long long wait_budget_ns;  // give up on the peers after this long
   unsigned int* err;               // device error word
 };

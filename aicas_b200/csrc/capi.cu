@@ -18,6 +18,7 @@ namespace aicas {
 
 struct DecodeArgs;
 cudaError_t launch_decode(int dtype, int head_dim, int group, const DecodeArgs& a, cudaStream_t st);
+cudaError_t launch_decode_exchange(int dtype, int group, const DecodeArgs& a, cudaStream_t st);
 int decode_tile_for(int dtype, int head_dim);
 struct RopeArgs;
 cudaError_t launch_rope_append(int dtype, int cs_dtype, const RopeArgs& a, cudaStream_t st);
@@ -413,9 +414,10 @@ size_t aicas_decode_workspace_bytes(const aicas_decode_params* p) {
   return plan.ws_bytes;
 }
 
-// Launches the decode of a checked call with its plan.
+// Launches the decode of a checked call with its plan (with the cross-GPU merge
+// fused in when a checked peer group is given).
 int run_decode(const aicas_decode_params* p, const DecodePlan& plan, void* workspace, size_t workspace_bytes,
-               void* stream) {
+               void* stream, const aicas_peer_group* group = nullptr) {
   if (plan.ws_bytes > 0 && (workspace == nullptr || workspace_bytes < plan.ws_bytes))
     return fail(AICAS_ERR_WORKSPACE, "decode needs %zu bytes of zero-initialised workspace (got %zu)", plan.ws_bytes,
                 workspace_bytes);
@@ -440,8 +442,27 @@ int run_decode(const aicas_decode_params* p, const DecodePlan& plan, void* works
   a.ws_count = plan.ws_bytes ? reinterpret_cast<unsigned int*>(ws + plan.ws_count_off) : nullptr;
   a.ws_sched = plan.ws_bytes ? reinterpret_cast<unsigned int*>(ws + kSchedOffset) : nullptr;
   a.err = device_error_word();
-  cudaError_t e = aicas::launch_decode(p->dtype, p->head_dim, p->num_q_heads / p->num_kv_heads, a,
-                                       static_cast<cudaStream_t>(stream));
+  memset(a.xpeers, 0, sizeof(a.xpeers));
+  a.xworld = a.xrank = 0;
+  a.xslot_floats = a.xslot_off = 0;
+  a.xbudget = 0;
+  cudaError_t e;
+  if (group != nullptr) {
+    for (int r = 0; r < group->world; ++r) a.xpeers[r] = group->peers[r];
+    a.xworld = group->world;
+    a.xrank = group->rank;
+    a.xslot_floats = (long long)aicas::exchange_slot_floats(p->batch, p->num_q_heads, p->head_dim);
+    a.xslot_off = aicas::exchange_slots_offset(p->batch, p->num_q_heads);
+    a.xbudget = group->wait_budget_ns != 0 ? group->wait_budget_ns : aicas::kWaitBudgetNs;
+    // the finalize phase claims pairs from the schedule counters, which every plan has here
+    a.ws_sched = reinterpret_cast<unsigned int*>(ws + kSchedOffset);
+    a.ws_count = reinterpret_cast<unsigned int*>(ws + plan.ws_count_off);
+    e = aicas::launch_decode_exchange(p->dtype, p->num_q_heads / p->num_kv_heads, a,
+                                      static_cast<cudaStream_t>(stream));
+  } else {
+    e = aicas::launch_decode(p->dtype, p->head_dim, p->num_q_heads / p->num_kv_heads, a,
+                             static_cast<cudaStream_t>(stream));
+  }
   if (e != cudaSuccess) return cuda_fail(e, "decode launch");
   return AICAS_OK;
 }
@@ -581,11 +602,45 @@ int aicas_exchange_merge(const aicas_exchange_params* p, void* stream) {
   a.heads = p->num_heads;
   a.hd = p->head_dim;
   a.slot_floats = (int)aicas::exchange_slot_floats(p->batch, p->num_heads, p->head_dim);
+  a.slot_off = aicas::exchange_slots_offset(p->batch, p->num_heads);
   a.wait_budget_ns = p->wait_budget_ns != 0 ? p->wait_budget_ns : aicas::kWaitBudgetNs;
   a.err = device_error_word();
   const cudaError_t e = aicas::launch_exchange_merge(p->dtype, a, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "exchange merge launch");
   return AICAS_OK;
+}
+
+size_t aicas_decode_exchange_workspace_bytes(const aicas_decode_params* p) {
+  if (check_decode(p) != AICAS_OK) return 0;
+  DecodePlan plan;
+  if (plan_decode(p, &plan) != AICAS_OK) return 0;
+  return std::max(plan.ws_bytes, kCounterBytes);
+}
+
+int aicas_decode_gqa_exchange(const aicas_decode_params* p, const aicas_peer_group* group, void* workspace,
+                              size_t workspace_bytes, void* stream) {
+  int rc = check_decode(p);
+  if (rc != AICAS_OK) return rc;
+  if (group == nullptr) return fail(AICAS_ERR_INVALID, "group is NULL");
+  if (group->world < 1 || group->world > AICAS_MAX_EXCHANGE_RANKS || group->rank < 0 || group->rank >= group->world)
+    return fail(AICAS_ERR_INVALID, "rank %d of world %d (at most %d ranks)", group->rank, group->world,
+                AICAS_MAX_EXCHANGE_RANKS);
+  for (int r = 0; r < group->world; ++r)
+    if (group->peers[r] == nullptr || (reinterpret_cast<uintptr_t>(group->peers[r]) & 255u) != 0)
+      return fail(AICAS_ERR_INVALID, "exchange buffer of rank %d is NULL or not 256-byte aligned", r);
+  if (p->out == nullptr || p->partial_o != nullptr)
+    return fail(AICAS_ERR_INVALID, "the fused exchange writes the merged out (and lse): out must be set, partial_o NULL");
+  if (p->head_dim != 128 || (p->dtype != AICAS_DTYPE_F16 && p->dtype != AICAS_DTYPE_BF16))
+    return fail(AICAS_ERR_UNSUPPORTED, "the fused exchange takes 16-bit caches with head_dim 128 (got dtype %d, %d)",
+                p->dtype, p->head_dim);
+  DecodePlan plan;
+  rc = plan_decode(p, &plan);
+  if (rc != AICAS_OK) return rc;
+  const size_t need = std::max(plan.ws_bytes, kCounterBytes);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(AICAS_ERR_WORKSPACE, "the fused exchange needs %zu bytes of zero-initialised workspace (got %zu)", need,
+                workspace_bytes);
+  return run_decode(p, plan, workspace, workspace_bytes, stream, group);
 }
 
 int aicas_rope_kv_append(const aicas_rope_append_params* p, void* stream) {

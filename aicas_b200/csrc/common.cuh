@@ -25,6 +25,17 @@ __device__ __forceinline__ unsigned long long global_timer_ns() {
   return t;
 }
 
+// Release store / acquire load at system scope: a flag that another GPU reads
+// (or writes) over NVLink, ordering the data written before it.
+__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // Sets AICAS_DEVERR_* bits in the library's device error word (its address is
 // passed to every kernel; see aicas_device_error_flags).
 __device__ __forceinline__ void flag_device_error(unsigned int* err, unsigned int bits) {

@@ -97,8 +97,31 @@ __device__ __forceinline__ bool consumer_any(bool pred) {
 // resets the pair's split counter for the next call; run by the consumer
 // threads of the CTA whose increment of that counter came last.  Up to eight
 // splits' partials are loaded before any is used (one L2 round trip).
-template <typename T, int D, int G, int kThreads>
-__device__ void merge_splits(const DecodeArgs& a, int b, int kvh, int nsplit) {
+// Where a (request, KV head) pair's result goes: the output (and/or the fp32
+// partial + LSE) of this device, or, with the cross-GPU merge fused in (XCHG),
+// this rank's slot in every rank's exchange buffer (the finalize phase of each
+// rank merges the ranks' results).
+template <typename T, int D, bool XCHG>
+__device__ __forceinline__ void pair_result(const DecodeArgs& a, int b, int qh, int d, float ov, float lse, int par) {
+  if constexpr (XCHG) {
+    const int64_t bh = (int64_t)b * a.hq + qh;
+    const int64_t n_o = (int64_t)a.batch * a.hq * D;
+    for (int r = 0; r < a.xworld; ++r) {
+      float* slot = reinterpret_cast<float*>(static_cast<uint8_t*>(a.xpeers[r]) + a.xslot_off) +
+                    ((int64_t)par * a.xworld + a.xrank) * a.xslot_floats;
+      slot[bh * D + d] = ov;
+      if (d == 0) slot[n_o + bh] = lse;
+    }
+  } else {
+    if (a.out != nullptr)
+      static_cast<T*>(a.out)[(int64_t)b * a.o_sb + (int64_t)qh * a.o_sh + d] = Elem<T>::from_float(ov);
+    if (a.partial_o != nullptr) a.partial_o[((int64_t)b * a.hq + qh) * D + d] = ov;
+    if (a.lse != nullptr && d == 0) a.lse[(int64_t)b * a.hq + qh] = lse;
+  }
+}
+
+template <typename T, int D, int G, int kThreads, bool XCHG>
+__device__ void merge_splits(const DecodeArgs& a, int b, int kvh, int nsplit, int par) {
   constexpr int kMC = 8;
   const int bh = b * a.hkv + kvh;
   for (int idx = threadIdx.x; idx < G * D; idx += kThreads) {
@@ -134,13 +157,18 @@ __device__ void merge_splits(const DecodeArgs& a, int b, int kvh, int nsplit) {
     }
     const float ov = (L > 0.f) ? O / L : 0.f;
     const float lse = (L > 0.f) ? M + log2f(L) : -INFINITY;
-    const int qh = kvh * G + h;
-    if (a.out != nullptr)
-      static_cast<T*>(a.out)[(int64_t)b * a.o_sb + (int64_t)qh * a.o_sh + d] = Elem<T>::from_float(ov);
-    if (a.partial_o != nullptr) a.partial_o[((int64_t)b * a.hq + qh) * D + d] = ov;
-    if (a.lse != nullptr && d == 0) a.lse[(int64_t)b * a.hq + qh] = lse;
+    pair_result<T, D, XCHG>(a, b, kvh * G + h, d, ov, lse, par);
   }
   if (threadIdx.x == 0) a.ws_count[bh] = 0u;  // ready for the next call
+}
+
+// XCHG: publishes a pair's result to every rank (after this CTA's consumer
+// threads have written it, fenced at system scope and passed a barrier).
+__device__ __forceinline__ void publish_pair(const DecodeArgs& a, int pair, unsigned long long e) {
+  for (int r = 0; r < a.xworld; ++r)
+    st_release_sys(reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(a.xpeers[r]) + kExchangePairFlags) +
+                       (int64_t)pair * 8 + a.xrank,
+                   e);
 }
 
 // Persistent CTAs (as many as fit on the device at once) run through the
@@ -151,7 +179,15 @@ __device__ void merge_splits(const DecodeArgs& a, int b, int kvh, int nsplit) {
 // copied by TMA), and streams its K/V tiles into a ring that runs on across
 // items, so the copies for the next item are in flight while the consumers
 // finish the current one.
-template <typename T, int D, int G>
+//
+// XCHG (the cross-GPU merge of a sequence-sharded cache fused in): each pair's
+// result goes straight into this rank's slot of every rank's exchange buffer,
+// with a per-pair flag; once a CTA's own item queue is drained it claims pairs
+// from a second counter, waits (bounded) until every rank has published that
+// pair and merges the ranks' results into the output.  No CTA waits for
+// another GPU while it holds a claimed item, so ranks cannot wait on each
+// other in a cycle; the last CTA out advances the buffer's epoch.
+template <typename T, int D, int G, bool XCHG>
 __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kThreads, G <= 2 ? 2 : 1)
     decode_gqa_kernel(const DecodeArgs a) {
   using C = DecodeCfg<T, D, G>;
@@ -213,6 +249,14 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kThreads, G <= 2 ? 2 : 1)
     }
   }
   grid_dependency_wait();
+  // XCHG: this call's epoch and slot parity (every CTA reads the epoch before
+  // the last CTA out advances it)
+  unsigned long long xe = 0;
+  int xpar = 0;
+  if constexpr (XCHG) {
+    xe = *reinterpret_cast<volatile unsigned long long*>(static_cast<uint8_t*>(a.xpeers[a.xrank]) + 256) + 1;
+    xpar = (int)(xe & 1);
+  }
 
   if (warp == C::kWarps) {
     // ------------------------------------------------------------ producer
@@ -510,22 +554,28 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kThreads, G <= 2 ? 2 : 1)
         const float lse = (L > 0.f) ? M + log2f(L) : -INFINITY;
         const int qh = it.kvh * G + h;
         if (single) {
-          if (a.out != nullptr)
-            static_cast<T*>(a.out)[(int64_t)it.b * a.o_sb + (int64_t)qh * a.o_sh + d] = Elem<T>::from_float(ov);
-          if (a.partial_o != nullptr) a.partial_o[((int64_t)it.b * a.hq + qh) * D + d] = ov;
-          if (a.lse != nullptr && d == 0) a.lse[(int64_t)it.b * a.hq + qh] = lse;
+          pair_result<T, D, XCHG>(a, it.b, qh, d, ov, lse, xpar);
         } else {
           a.ws_o[(((int64_t)bh * a.max_splits + it.split) * G + h) * D + d] = ov;
           if (d == 0) a.ws_lse[((int64_t)bh * a.max_splits + it.split) * G + h] = lse;
         }
       }
-      if (s_merge[0]) merge_splits<T, D, G, C::kWarps * 32>(a, s_merge[1], s_merge[2], s_merge[3]);
+      if (s_merge[0]) merge_splits<T, D, G, C::kWarps * 32, XCHG>(a, s_merge[1], s_merge[2], s_merge[3], xpar);
+      if constexpr (XCHG) {
+        if (single || s_merge[0]) __threadfence_system();  // this CTA's results reach every rank first
+      }
       // the reductions buffer and s_merge are reused by the next item; for a
       // split this barrier also orders the CTA's partial writes before thread
       // 0's acquire-release increment of the pair's split counter at GPU scope
       // (cumulative), which in turn orders every split's partials before the
       // merge that the last increment triggers
       consumer_sync<C::kWarps>();
+      if constexpr (XCHG) {
+        if (threadIdx.x == 0) {
+          if (single) publish_pair(a, bh, xe);
+          if (s_merge[0]) publish_pair(a, s_merge[1] * a.hkv + s_merge[2], xe);
+        }
+      }
       if (!single && threadIdx.x == 0) {
         // issued now, read at the next item's end (or after the last item)
         asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(pend_prev) : "l"(a.ws_count + bh) : "memory");
@@ -537,7 +587,60 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kThreads, G <= 2 ? 2 : 1)
     // ---- the last item's increment: merge its pair if that came last
     if (threadIdx.x == 0) publish_pending();
     consumer_sync<C::kWarps>();
-    if (s_merge[0] && s_abort == 0) merge_splits<T, D, G, C::kWarps * 32>(a, s_merge[1], s_merge[2], s_merge[3]);
+    if (s_merge[0] && s_abort == 0)
+      merge_splits<T, D, G, C::kWarps * 32, XCHG>(a, s_merge[1], s_merge[2], s_merge[3], xpar);
+    if constexpr (XCHG) {
+      // ---- publish that pair, then finalize pairs: merge every rank's result
+      const bool merged = s_merge[0] && s_abort == 0;
+      if (merged) __threadfence_system();
+      consumer_sync<C::kWarps>();
+      if (merged && threadIdx.x == 0) publish_pair(a, s_merge[1] * a.hkv + s_merge[2], xe);
+      __shared__ int s_fin[2];  // [pair claimed, a peer did not arrive]
+      const int pairs = a.batch * a.hkv;
+      uint8_t* own = static_cast<uint8_t*>(a.xpeers[a.xrank]);
+      const unsigned long long* pflags = reinterpret_cast<const unsigned long long*>(own + kExchangePairFlags);
+      const float* slots = reinterpret_cast<const float*>(own + a.xslot_off) + (int64_t)xpar * a.xworld * a.xslot_floats;
+      const int64_t n_o = (int64_t)a.batch * a.hq * D;
+      for (;;) {
+        if (threadIdx.x == 0) {
+          s_fin[0] = s_abort ? pairs : (int)atomicAdd(a.ws_sched + 2, 1u);
+          s_fin[1] = 0;
+        }
+        consumer_sync<C::kWarps>();
+        const int pair = s_fin[0];
+        if (pair >= pairs) break;  // every consumer thread read the same value
+        if (threadIdx.x < a.xworld) {
+          const unsigned long long t0 = global_timer_ns();
+          for (uint32_t it = 1; ld_acquire_sys(pflags + (int64_t)pair * 8 + threadIdx.x) < xe; ++it) {
+            if ((it & 63u) == 0u && global_timer_ns() - t0 > a.xbudget) {
+              flag_device_error(a.err, AICAS_DEVERR_PEER_TIMEOUT);
+              s_fin[1] = 1;
+              break;
+            }
+          }
+        }
+        consumer_sync<C::kWarps>();
+        const int b = pair / a.hkv, kvh = pair % a.hkv;
+        for (int idx = threadIdx.x; idx < G * D; idx += C::kWarps * 32) {
+          const int h = idx / D, d = idx % D, qh = kvh * G + h;
+          const int64_t bh = (int64_t)b * a.hq + qh;
+          float M = -INFINITY;
+          for (int r = 0; r < a.xworld && !s_fin[1]; ++r) M = fmaxf(M, __ldcv(slots + (int64_t)r * a.xslot_floats + n_o + bh));
+          float L = 0.f, O = 0.f;
+          if (M != -INFINITY)
+            for (int r = 0; r < a.xworld; ++r) {
+              const float* sr = slots + (int64_t)r * a.xslot_floats;
+              const float w = exp2f(__ldcv(sr + n_o + bh) - M);
+              L += w;
+              O = fmaf(w, __ldcv(sr + bh * D + d), O);
+            }
+          if (a.out != nullptr)
+            static_cast<T*>(a.out)[(int64_t)b * a.o_sb + (int64_t)qh * a.o_sh + d] = Elem<T>::from_float(L > 0.f ? O / L : 0.f);
+          if (a.lse != nullptr && d == 0) a.lse[bh] = L > 0.f ? M + log2f(L) : -INFINITY;
+        }
+        consumer_sync<C::kWarps>();  // s_fin is reused by the next claim
+      }
+    }
   }
 
   // ---- scheduling counters back to zero for the next call: the last CTA out resets them
@@ -549,6 +652,11 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kThreads, G <= 2 ? 2 : 1)
       if (done == gridDim.x - 1) {
         a.ws_sched[0] = 0u;
         a.ws_sched[1] = 0u;
+        if constexpr (XCHG) {
+          a.ws_sched[2] = 0u;
+          // this call is complete on this rank
+          *reinterpret_cast<volatile unsigned long long*>(static_cast<uint8_t*>(a.xpeers[a.xrank]) + 256) = xe;
+        }
         __threadfence();
       }
     }
@@ -557,7 +665,7 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kThreads, G <= 2 ? 2 : 1)
 
 // ------------------------------------------------------------------ host side
 
-template <typename T, int D, int G>
+template <typename T, int D, int G, bool XCHG>
 static cudaError_t launch_decode_t(const DecodeArgs& a, cudaStream_t st) {
   using C = DecodeCfg<T, D, G>;
   // the dynamic shared-memory opt-in and the co-resident CTA count are per
@@ -568,11 +676,11 @@ static cudaError_t launch_decode_t(const DecodeArgs& a, cudaStream_t st) {
   if (e != cudaSuccess) return e;
   int per_device = (dev >= 0 && dev < 64) ? resident[dev] : 0;
   if (per_device == 0) {
-    e = cudaFuncSetAttribute(decode_gqa_kernel<T, D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(decode_gqa_kernel<T, D, G, XCHG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              C::kSmemBytes);
     if (e != cudaSuccess) return e;
     int per_sm = 0, sms = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_gqa_kernel<T, D, G>, C::kThreads,
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_gqa_kernel<T, D, G, XCHG>, C::kThreads,
                                                       C::kSmemBytes);
     if (e != cudaSuccess) return e;
     e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -588,16 +696,16 @@ static cudaError_t launch_decode_t(const DecodeArgs& a, cudaStream_t st) {
   DecodeArgs b = a;
   const long long first_bytes = (long long)grid * (a.split_tokens < a.cap ? a.split_tokens : a.cap) * 2 * C::kRowBytes;
   b.prefetch_first = (a.ws_sched != nullptr && first_bytes <= (64ll << 20)) ? 1 : 0;
-  return launch_pdl(decode_gqa_kernel<T, D, G>, dim3(grid), dim3(C::kThreads), C::kSmemBytes, st, b);
+  return launch_pdl(decode_gqa_kernel<T, D, G, XCHG>, dim3(grid), dim3(C::kThreads), C::kSmemBytes, st, b);
 }
 
-template <typename T, int D>
+template <typename T, int D, bool XCHG = false>
 static cudaError_t dispatch_g(int g, const DecodeArgs& a, cudaStream_t st) {
   switch (g) {
-    case 1: return launch_decode_t<T, D, 1>(a, st);
-    case 2: return launch_decode_t<T, D, 2>(a, st);
-    case 4: return launch_decode_t<T, D, 4>(a, st);
-    case 8: return launch_decode_t<T, D, 8>(a, st);
+    case 1: return launch_decode_t<T, D, 1, XCHG>(a, st);
+    case 2: return launch_decode_t<T, D, 2, XCHG>(a, st);
+    case 4: return launch_decode_t<T, D, 4, XCHG>(a, st);
+    case 8: return launch_decode_t<T, D, 8, XCHG>(a, st);
   }
   return cudaErrorInvalidValue;
 }
@@ -617,6 +725,16 @@ static cudaError_t dispatch_d(int d, int g, const DecodeArgs& a, cudaStream_t st
 int decode_tile_for(int dtype, int head_dim) {
   const int elem = dtype == AICAS_DTYPE_F32 ? 4 : 2;
   return 16384 / (head_dim * elem);
+}
+
+// The decode with the cross-GPU merge fused in: 16-bit caches at head_dim 128
+// (the sequence-sharded long-context decode of Qwen3-VL-2B's text decoder).
+cudaError_t launch_decode_exchange(int dtype, int group, const DecodeArgs& a, cudaStream_t st) {
+  switch (dtype) {
+    case AICAS_DTYPE_F16: return dispatch_g<__half, 128, true>(group, a, st);
+    case AICAS_DTYPE_BF16: return dispatch_g<__nv_bfloat16, 128, true>(group, a, st);
+  }
+  return cudaErrorInvalidValue;
 }
 
 cudaError_t launch_decode(int dtype, int head_dim, int group, const DecodeArgs& a, cudaStream_t st) {

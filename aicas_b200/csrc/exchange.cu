@@ -2,13 +2,10 @@
 // memory, in one kernel.
 //
 // Each rank owns an exchange buffer (the same size on every rank) that the
-// other ranks map through CUDA IPC:
-//   [0, 256)     uint64 flags[32]: flags[src] = last epoch rank src published here
-//   [256, 264)   uint64 epoch: calls completed by the owner (advanced on the device,
-//                so a captured graph replays correctly)
-//   [264, 268)   uint32 CTAs of the current call that have finished
-//   [512, ...)   fp32 slots[2][world][slot_floats]: the (out, lse) partial of each
-//                source rank, double-buffered by epoch parity
+// other ranks map through CUDA IPC; its layout is in args.cuh (flags, the epoch,
+// advanced on the device so a captured graph replays correctly, per-pair flags
+// of the fused decode, and the fp32 (out, lse) slots of every source rank,
+// double-buffered by epoch parity).
 // One CTA per destination rank: CTA p writes the local partial into slot
 // [parity][rank] of rank p's buffer (plain stores over NVLink, every
 // destination in parallel), fences at system scope and publishes the epoch
@@ -30,16 +27,7 @@ namespace aicas {
 namespace {
 
 constexpr int kExchangeThreads = 256;
-constexpr size_t kSlotOffset = 512;
 
-__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
-  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
 
 template <typename T>
 __global__ void __launch_bounds__(kExchangeThreads) exchange_merge_kernel(const ExchangeArgs a) {
@@ -60,7 +48,7 @@ __global__ void __launch_bounds__(kExchangeThreads) exchange_merge_kernel(const 
 
   // 1. publish the local partial into rank dst's buffer (own buffer for dst == rank)
   {
-    float* slot = reinterpret_cast<float*>(static_cast<uint8_t*>(a.peers[dst]) + kSlotOffset) +
+    float* slot = reinterpret_cast<float*>(static_cast<uint8_t*>(a.peers[dst]) + a.slot_off) +
                   ((size_t)par * a.world + a.rank) * a.slot_floats;
     const float4* src4 = reinterpret_cast<const float4*>(a.po);
     float4* dst4 = reinterpret_cast<float4*>(slot);
@@ -85,7 +73,7 @@ __global__ void __launch_bounds__(kExchangeThreads) exchange_merge_kernel(const 
   __syncthreads();
 
   // 3. merge this CTA's share of the rows: one thread per (row, 4 columns)
-  const float* slots = reinterpret_cast<const float*>(own + kSlotOffset) + (size_t)par * a.world * a.slot_floats;
+  const float* slots = reinterpret_cast<const float*>(own + a.slot_off) + (size_t)par * a.world * a.slot_floats;
   const int q4 = a.hd / 4;
   const int rows_per = (nbh + gridDim.x - 1) / gridDim.x;
   const int r0 = blockIdx.x * rows_per, r1 = min(nbh, r0 + rows_per);
@@ -143,7 +131,8 @@ size_t exchange_slot_floats(int batch, int heads, int head_dim) {
 }
 
 size_t exchange_buffer_bytes(int world, int batch, int heads, int head_dim) {
-  return kSlotOffset + 2 * (size_t)world * exchange_slot_floats(batch, heads, head_dim) * sizeof(float);
+  return (size_t)exchange_slots_offset(batch, heads) +
+         2 * (size_t)world * exchange_slot_floats(batch, heads, head_dim) * sizeof(float);
 }
 
 cudaError_t launch_exchange_merge(int dtype, const ExchangeArgs& a, cudaStream_t st) {

@@ -109,7 +109,25 @@ class PeerExchange:
                 self._opened.append(ptr.value)
                 peers.append(ptr.value)
         self._peers = peers
+        self._group = _native.PeerGroup()
+        for r, ptr in enumerate(peers):
+            self._group.peers[r] = ptr
+        self._group.world, self._group.rank = self.world, self.rank
         dist.barrier(group=group)
+
+    def decode(self, query: torch.Tensor, key_shard: torch.Tensor, value_shard: torch.Tensor, *, sm_scale: float,
+               num_key_value_groups: int, kv_lens_local: torch.Tensor | None = None) -> torch.Tensor:
+        """The sharded decode with the exchange fused into the decode kernel
+        (one launch per rank, no partials in HBM): every rank returns the merged
+        ``[B, Hq, 1, D]`` output.  Collective, like :meth:`merge`, and shares its
+        buffers."""
+        B, H, D = self.shape
+        if query.shape[0] != B or query.shape[1] != H or query.shape[-1] != D:
+            raise ValueError(f"query {tuple(query.shape)} does not match the exchange shape {self.shape}")
+        if self._own is None:
+            raise ValueError("the exchange is closed")
+        return ops.gqa_decode_exchange(query, key_shard, value_shard, self._group, sm_scale=sm_scale,
+                                       num_key_value_groups=num_key_value_groups, kv_lens=kv_lens_local)
 
     def merge(self, partial_o: torch.Tensor, partial_lse: torch.Tensor, out_dtype: torch.dtype) -> torch.Tensor:
         """All ranks' partials merged into a new ``[B, H, 1, D]`` tensor (every rank gets the full result)."""
@@ -159,11 +177,19 @@ def sharded_gqa_decode(
     kv_lens_local: torch.Tensor | None = None,
     group=None,
     exchange: PeerExchange | None = None,
+    fused: bool = False,
 ) -> torch.Tensor:
     """Decode attention over a cache sharded along the sequence across the ranks
     of `group`: partial on the local shard, then either the one-kernel peer
     exchange + merge (`exchange` given) or one NCCL all-gather and the merge
-    kernel.  Every rank returns the full ``[B, Hq, 1, D]`` output."""
+    kernel.  With `exchange` and `fused`, the decode kernel itself exchanges and
+    merges (:meth:`PeerExchange.decode`).  Every rank returns the full
+    ``[B, Hq, 1, D]`` output."""
+    if fused:
+        if exchange is None:
+            raise ValueError("the fused exchange needs a PeerExchange")
+        return exchange.decode(query, key_shard, value_shard, sm_scale=sm_scale,
+                               num_key_value_groups=num_key_value_groups, kv_lens_local=kv_lens_local)
     po, lse = ops.gqa_decode_partial(query, key_shard, value_shard, sm_scale=sm_scale,
                                      num_key_value_groups=num_key_value_groups, kv_lens=kv_lens_local)
     if exchange is not None:

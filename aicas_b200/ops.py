@@ -146,7 +146,7 @@ def _check_decode(query, key, value, num_key_value_groups: int) -> None:
 
 
 def _decode_call(query, key, value, *, sm_scale, num_key_value_groups, kv_lens, split_tokens, out, lse, partial_o,
-                 kv_starts=None):
+                 kv_starts=None, group=None):
     B, Hq, _, D = query.shape
     Hkv, L = key.shape[1], key.shape[2]
     device = query.device
@@ -171,6 +171,14 @@ def _decode_call(query, key, value, *, sm_scale, num_key_value_groups, kv_lens, 
     def run():
         lib = nat.lib()
         stream = _stream_handle(device)
+        if group is not None:
+            # the decode with the cross-GPU merge fused in (group: nat.PeerGroup)
+            nbytes = int(lib.aicas_decode_exchange_workspace_bytes(ctypes.byref(p)))
+            ws = _workspace(device, stream, nbytes) if nbytes > 0 else None
+            rc = lib.aicas_decode_gqa_exchange(ctypes.byref(p), ctypes.byref(group), _ptr(ws),
+                                               ws.numel() if ws is not None else 0, stream)
+            nat.check(rc, "aicas_decode_gqa_exchange")
+            return
         nbytes = int(lib.aicas_decode_workspace_bytes(ctypes.byref(p)))
         ws = _workspace(device, stream, nbytes) if nbytes > 0 else None
         rc = lib.aicas_decode_gqa(ctypes.byref(p), _ptr(ws), ws.numel() if ws is not None else 0, stream)
@@ -241,6 +249,34 @@ def gqa_decode_partial(
     _decode_call(query, key, value, sm_scale=sm_scale, num_key_value_groups=num_key_value_groups, kv_lens=lens,
                  split_tokens=split_tokens, out=None, lse=lse, partial_o=po)
     return po, lse
+
+
+def gqa_decode_exchange(
+    query: torch.Tensor,
+    key: torch.Tensor,
+    value: torch.Tensor,
+    group,
+    *,
+    sm_scale: float,
+    num_key_value_groups: int,
+    kv_lens: torch.Tensor | Sequence[int] | None = None,
+    split_tokens: int = 0,
+) -> torch.Tensor:
+    """Decode over this rank's shard of a sequence-sharded cache with the
+    cross-GPU merge fused into the decode kernel (``group``: the ranks' exchange
+    buffers as a ``_native.PeerGroup``).  Collective; every rank returns the
+    merged ``[B, Hq, 1, D]`` output.  16-bit caches, head_dim 128."""
+    _reject_grad(query, key, value)
+    _check_decode(query, key, value, num_key_value_groups)
+    B, Hq, _, D = query.shape
+    query = _heads_ready(query)
+    key = _rows_ready(key)
+    value = _rows_ready(value)
+    lens = _as_lens(kv_lens, B, query.device)
+    out = torch.empty((B, 1, Hq, D), dtype=query.dtype, device=query.device).transpose(1, 2)
+    _decode_call(query, key, value, sm_scale=sm_scale, num_key_value_groups=num_key_value_groups, kv_lens=lens,
+                 split_tokens=split_tokens, out=out, lse=None, partial_o=None, group=group)
+    return out
 
 
 def merge_partials(

@@ -212,6 +212,28 @@ typedef struct aicas_exchange_params {
 
 AICAS_API int aicas_exchange_merge(const aicas_exchange_params* p, void* stream);
 
+/* The sequence-sharded decode with the exchange fused into the decode kernel:
+   every rank decodes its shard of every cache (p: out = the merged [B, Hq, 1, D]
+   output, lse = the optional merged LSE, partial_o = NULL) and each (request,
+   KV head) result goes straight into every rank's exchange buffer; a CTA whose
+   own work is done merges pairs whose results have arrived from every rank.
+   Replaces aicas_decode_gqa(partial_o) + aicas_exchange_merge (one launch, no
+   partials in HBM).  The buffers are the exchange buffers of
+   aicas_exchange_buffer_bytes(world, batch, num_q_heads, head_dim), shared with
+   aicas_exchange_merge; 16-bit caches, head_dim 128.  Collective: every rank
+   calls it in the same order.  The workspace (zero-initialised once, left zeroed
+   by every call) is aicas_decode_exchange_workspace_bytes(p) bytes or more. */
+typedef struct aicas_peer_group {
+  void* peers[AICAS_MAX_EXCHANGE_RANKS]; /* rank r's exchange buffer as mapped here (own buffer at [rank]) */
+  int32_t world, rank;
+  uint64_t wait_budget_ns;  /* bound of the wait for the peers' results (sets AICAS_DEVERR_PEER_TIMEOUT,
+                               writes zeros); 0 = 4 s */
+} aicas_peer_group;
+
+AICAS_API size_t aicas_decode_exchange_workspace_bytes(const aicas_decode_params* p);
+AICAS_API int aicas_decode_gqa_exchange(const aicas_decode_params* p, const aicas_peer_group* group,
+                                        void* workspace, size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Flash attention on the tensor cores (tcgen05): causal GQA prefill and     */
 /* non-causal packed-varlen attention.                                       */

@@ -52,6 +52,8 @@ STRUCTS = {
     "aicas_linear_segment": nat.LinearSegment,
     "aicas_linear_params": nat.LinearParams,
     "aicas_vision_rope_params": nat.VisionRopeParams,
+    "aicas_vision_qkv_params": nat.VisionQkvParams,
+    "aicas_peer_group": nat.PeerGroup,
 }
 
 
@@ -191,10 +193,13 @@ def test_merge_validation(native_lib):
 
 
 def test_exchange_buffer_size_and_validation(native_lib):
-    # header + 2 parities x world slots of B*H*(D+1) floats rounded up to 4
+    # header (flags, epoch, then 8 per-pair flags of 8 bytes for each of the B*H
+    # pairs, rounded up to 256 bytes) + 2 parities x world slots of B*H*(D+1)
+    # floats rounded up to 4
     slot = (4 * 16 * 129 + 3) // 4 * 4
-    assert native_lib.aicas_exchange_buffer_bytes(2, 4, 16, 128) == 512 + 2 * 2 * slot * 4
-    assert native_lib.aicas_exchange_buffer_bytes(8, 4, 16, 128) == 512 + 2 * 8 * slot * 4
+    header = (512 + 4 * 16 * 64 + 255) // 256 * 256
+    assert native_lib.aicas_exchange_buffer_bytes(2, 4, 16, 128) == header + 2 * 2 * slot * 4
+    assert native_lib.aicas_exchange_buffer_bytes(8, 4, 16, 128) == header + 2 * 8 * slot * 4
     assert native_lib.aicas_exchange_buffer_bytes(9, 4, 16, 128) == 0  # more ranks than the kernel takes
     assert native_lib.aicas_exchange_buffer_bytes(2, 0, 16, 128) == 0
     p = nat.ExchangeParams()
@@ -215,6 +220,38 @@ def test_exchange_buffer_size_and_validation(native_lib):
     assert "multiple of 4" in nat.last_error()
     assert native_lib.aicas_peer_buffer_alloc(0, None, None) == nat.ERR_INVALID
     assert native_lib.aicas_peer_buffer_open(None, None) == nat.ERR_INVALID
+
+
+def test_fused_exchange_validation(native_lib):
+    p = _decode_params()
+    g = nat.PeerGroup()
+    call = lambda: native_lib.aicas_decode_gqa_exchange(ctypes.byref(p), ctypes.byref(g), 1 << 20, 1 << 20, None)
+    assert native_lib.aicas_decode_gqa_exchange(ctypes.byref(p), None, None, 0, None) == nat.ERR_INVALID
+    assert "group is NULL" in nat.last_error()
+    g.world, g.rank = 2, 2
+    assert call() == nat.ERR_INVALID and "rank 2 of world 2" in nat.last_error()
+    g.world, g.rank = 9, 0
+    assert call() == nat.ERR_INVALID and "at most 8 ranks" in nat.last_error()
+    g.world, g.rank = 2, 0
+    g.peers[0], g.peers[1] = 4 << 20, (5 << 20) + 64
+    assert call() == nat.ERR_INVALID and "256-byte aligned" in nat.last_error()
+    g.peers[1] = 5 << 20
+    p.partial_o, p.lse = 6 << 20, 7 << 20
+    assert call() == nat.ERR_INVALID and "partial_o NULL" in nat.last_error()
+    p.partial_o = None
+    p.head_dim = 64
+    assert call() == nat.ERR_UNSUPPORTED and "head_dim 128" in nat.last_error()
+    p.head_dim, p.dtype = 128, nat.DTYPE_F32
+    assert call() == nat.ERR_UNSUPPORTED and "16-bit" in nat.last_error()
+    # the workspace holds at least the scheduling counters (1 MiB), else the split-KV plan's size
+    p.dtype = nat.DTYPE_BF16
+    plain = native_lib.aicas_decode_workspace_bytes(ctypes.byref(p))
+    assert native_lib.aicas_decode_exchange_workspace_bytes(ctypes.byref(p)) == max(plain, 1 << 20)
+    p2 = _decode_params(split_tokens=4096)
+    assert native_lib.aicas_decode_workspace_bytes(ctypes.byref(p2)) == 0
+    assert native_lib.aicas_decode_exchange_workspace_bytes(ctypes.byref(p2)) == 1 << 20
+    assert native_lib.aicas_decode_gqa_exchange(ctypes.byref(p2), ctypes.byref(g), 1 << 20, (1 << 20) - 1,
+                                                None) == nat.ERR_WORKSPACE
 
 
 def _linear_params(R=8, K=2048, rows=(2048, 1024, 1024), mode=nat.LINEAR_STORE) -> nat.LinearParams:

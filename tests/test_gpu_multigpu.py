@@ -1,7 +1,9 @@
 """Sequence-sharded (split-KV) decode across real GPUs: each rank runs the
 partial decode kernel on its shard of the cache, then the partials are
 combined either by the one-kernel NVLink peer exchange + merge or by one NCCL
-all-gather and the merge kernel.  Checked on every rank against the fp64
+all-gather and the merge kernel; or the decode kernel itself exchanges and
+merges (the fused path, whose middle call goes through the merge kernel on the
+same buffers so the two share the epoch).  Checked on every rank against the fp64
 oracle of the whole cache (tolerance: the north-star bf16 bar, max-abs 2e-2
 and mean-abs 2e-3); the peer path runs three calls in a row so both parities
 of its double-buffered slots, and their reuse, are exercised.
@@ -43,7 +45,7 @@ def _worker(rank: int, world: int, port: int, path: str, cases, out_dir: str):
     exchange = None
     try:
         q0 = cases[0][0]
-        if path == "peer":
+        if path in ("peer", "fused"):
             exchange = adist.PeerExchange(q0.shape[0], q0.shape[1], q0.shape[3], device)
         for i, (q, k, v, lens) in enumerate(cases):
             L = k.shape[2]
@@ -53,7 +55,8 @@ def _worker(rank: int, world: int, port: int, path: str, cases, out_dir: str):
             vd = v[:, :, s0:s1].contiguous().to(device)
             local = adist.local_lengths(lens, s0, s1).to(device)
             out = adist.sharded_gqa_decode(qd, kd, vd, sm_scale=q.shape[-1] ** -0.5, num_key_value_groups=2,
-                                           kv_lens_local=local, exchange=exchange)
+                                           kv_lens_local=local, exchange=exchange,
+                                           fused=(path == "fused" and i != 1))
             torch.cuda.synchronize(device)
             np.save(os.path.join(out_dir, f"out{rank}_{i}.npy"), out.float().cpu().numpy())
         from aicas_b200 import _native
@@ -66,7 +69,7 @@ def _worker(rank: int, world: int, port: int, path: str, cases, out_dir: str):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("path", ["peer", "nccl"])
+@pytest.mark.parametrize("path", ["peer", "fused", "nccl"])
 @pytest.mark.parametrize("world", [2, 4, 8])
 def test_split_kv_decode_across_gpus(tmp_path, world, path):
     if torch.cuda.device_count() < world:
