@@ -587,6 +587,11 @@ int aicas_exchange_merge(const aicas_exchange_params* p, void* stream) {
     return fail(AICAS_ERR_INVALID, "bad sizes (head_dim must be a multiple of 4)");
   if ((reinterpret_cast<uintptr_t>(p->partial_o) & 15u) != 0)
     return fail(AICAS_ERR_INVALID, "partial_o must be 16-byte aligned");
+  {
+    const int64_t eb = elem_bytes(p->dtype);
+    if ((reinterpret_cast<uintptr_t>(p->out) & 15u) != 0 || (p->o_stride_b * eb) % 16 != 0 || (p->o_stride_h * eb) % 16 != 0)
+      return fail(AICAS_ERR_INVALID, "out must be 16-byte aligned with strides that are multiples of 16 bytes");
+  }
   aicas::ExchangeArgs a;
   memset(&a, 0, sizeof(a));
   for (int r = 0; r < p->world; ++r) a.peers[r] = p->peers[r];

@@ -25,14 +25,19 @@ __device__ __forceinline__ unsigned long long global_timer_ns() {
   return t;
 }
 
-// Release store / acquire load at system scope: a flag that another GPU reads
-// (or writes) over NVLink, ordering the data written before it.
-__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
-  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+// Flags that another GPU reads (or writes) over NVLink.  Publishing: the
+// writers of the data pass a barrier, then one thread fences at system scope
+// (cumulative over the writes the barrier ordered before it) and stores the
+// flag relaxed: a release pattern with one fence for the whole CTA.  Waiting:
+// relaxed polls, then one system-scope fence (an acquire pattern), so a poll
+// costs no fence.
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ void st_relaxed_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
-__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+__device__ __forceinline__ unsigned long long ld_relaxed_sys(const unsigned long long* p) {
   unsigned long long v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
 

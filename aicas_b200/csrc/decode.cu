@@ -162,11 +162,13 @@ __device__ void merge_splits(const DecodeArgs& a, int b, int kvh, int nsplit, in
   if (threadIdx.x == 0) a.ws_count[bh] = 0u;  // ready for the next call
 }
 
-// XCHG: publishes a pair's result to every rank (after this CTA's consumer
-// threads have written it, fenced at system scope and passed a barrier).
+// XCHG: publishes a pair's result to every rank, by one thread after this
+// CTA's consumer threads have written it and passed a barrier: one
+// system-scope fence (cumulative over their stores), then the flags.
 __device__ __forceinline__ void publish_pair(const DecodeArgs& a, int pair, unsigned long long e) {
+  fence_acq_rel_sys();
   for (int r = 0; r < a.xworld; ++r)
-    st_release_sys(reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(a.xpeers[r]) + kExchangePairFlags) +
+    st_relaxed_sys(reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(a.xpeers[r]) + kExchangePairFlags) +
                        (int64_t)pair * 8 + a.xrank,
                    e);
 }
@@ -561,9 +563,6 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kThreads, G <= 2 ? 2 : 1)
         }
       }
       if (s_merge[0]) merge_splits<T, D, G, C::kWarps * 32, XCHG>(a, s_merge[1], s_merge[2], s_merge[3], xpar);
-      if constexpr (XCHG) {
-        if (single || s_merge[0]) __threadfence_system();  // this CTA's results reach every rank first
-      }
       // the reductions buffer and s_merge are reused by the next item; for a
       // split this barrier also orders the CTA's partial writes before thread
       // 0's acquire-release increment of the pair's split counter at GPU scope
@@ -592,7 +591,6 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kThreads, G <= 2 ? 2 : 1)
     if constexpr (XCHG) {
       // ---- publish that pair, then finalize pairs: merge every rank's result
       const bool merged = s_merge[0] && s_abort == 0;
-      if (merged) __threadfence_system();
       consumer_sync<C::kWarps>();
       if (merged && threadIdx.x == 0) publish_pair(a, s_merge[1] * a.hkv + s_merge[2], xe);
       __shared__ int s_fin[2];  // [pair claimed, a peer did not arrive]
@@ -611,29 +609,41 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kThreads, G <= 2 ? 2 : 1)
         if (pair >= pairs) break;  // every consumer thread read the same value
         if (threadIdx.x < a.xworld) {
           const unsigned long long t0 = global_timer_ns();
-          for (uint32_t it = 1; ld_acquire_sys(pflags + (int64_t)pair * 8 + threadIdx.x) < xe; ++it) {
+          for (uint32_t it = 1; ld_relaxed_sys(pflags + (int64_t)pair * 8 + threadIdx.x) < xe; ++it) {
             if ((it & 63u) == 0u && global_timer_ns() - t0 > a.xbudget) {
               flag_device_error(a.err, AICAS_DEVERR_PEER_TIMEOUT);
               s_fin[1] = 1;
               break;
             }
           }
+          fence_acq_rel_sys();
         }
         consumer_sync<C::kWarps>();
         const int b = pair / a.hkv, kvh = pair % a.hkv;
         for (int idx = threadIdx.x; idx < G * D; idx += C::kWarps * 32) {
           const int h = idx / D, d = idx % D, qh = kvh * G + h;
           const int64_t bh = (int64_t)b * a.hq + qh;
+          // L2 reads (this SM's L1 may hold the slot from two calls ago), all
+          // ranks' loads issued together
+          float lr[kMaxExchangeRanks], orr[kMaxExchangeRanks];
           float M = -INFINITY;
-          for (int r = 0; r < a.xworld && !s_fin[1]; ++r) M = fmaxf(M, __ldcv(slots + (int64_t)r * a.xslot_floats + n_o + bh));
+#pragma unroll
+          for (int r = 0; r < kMaxExchangeRanks; ++r) {
+            const bool in = r < a.xworld && !s_fin[1];
+            const float* sr = slots + (int64_t)r * a.xslot_floats;
+            lr[r] = in ? __ldcg(sr + n_o + bh) : -INFINITY;
+            orr[r] = in ? __ldcg(sr + bh * D + d) : 0.f;
+            M = fmaxf(M, lr[r]);
+          }
           float L = 0.f, O = 0.f;
-          if (M != -INFINITY)
-            for (int r = 0; r < a.xworld; ++r) {
-              const float* sr = slots + (int64_t)r * a.xslot_floats;
-              const float w = exp2f(__ldcv(sr + n_o + bh) - M);
+          if (M != -INFINITY) {
+#pragma unroll
+            for (int r = 0; r < kMaxExchangeRanks; ++r) {
+              const float w = exp2f(lr[r] - M);  // 0 for ranks past the world
               L += w;
-              O = fmaf(w, __ldcv(sr + bh * D + d), O);
+              O = fmaf(w, orr[r], O);
             }
+          }
           if (a.out != nullptr)
             static_cast<T*>(a.out)[(int64_t)b * a.o_sb + (int64_t)qh * a.o_sh + d] = Elem<T>::from_float(L > 0.f ? O / L : 0.f);
           if (a.lse != nullptr && d == 0) a.lse[bh] = L > 0.f ? M + log2f(L) : -INFINITY;

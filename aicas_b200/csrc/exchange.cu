@@ -8,11 +8,12 @@
 // double-buffered by epoch parity).
 // One CTA per destination rank: CTA p writes the local partial into slot
 // [parity][rank] of rank p's buffer (plain stores over NVLink, every
-// destination in parallel), fences at system scope and publishes the epoch
-// with a release store into rank p's flags[rank].  Every CTA then waits
-// (bounded) until all ranks' flags in its own buffer have reached the epoch
-// and merges its share of the (request, head) rows exactly as the
-// single-device merge does: o = sum_r 2^(lse_r - M) o_r / sum_r 2^(lse_r - M).
+// destination in parallel), passes a barrier, and one thread fences at system
+// scope and stores the epoch into rank p's flags[rank].  Every CTA then waits
+// (bounded, relaxed polls and one fence) until all ranks' flags in its own
+// buffer have reached the epoch and merges its share of the (request, head)
+// rows exactly as the single-device merge does:
+// o = sum_r 2^(lse_r - M) o_r / sum_r 2^(lse_r - M).
 // The last CTA to finish advances the epoch, so every CTA of a call reads the
 // same epoch whatever order they start in.
 //
@@ -20,13 +21,28 @@
 // in call e + 2, after its call e + 1 has seen every peer's flag for e + 1,
 // and each peer set that flag after its call e, which read parity p, had
 // finished (calls are ordered on each rank's stream).
+#include <type_traits>
+
 #include "common.cuh"
 #include "args.cuh"
 
 namespace aicas {
 namespace {
 
-constexpr int kExchangeThreads = 256;
+// 1024 threads: a CTA's push (one partial, 33 KB at config 5) and its share of
+// the merge take one or two memory round trips per thread
+constexpr int kExchangeThreads = 1024;
+
+// four consecutive outputs in one store (8 bytes for 16-bit types)
+template <typename T>
+__device__ __forceinline__ void store4(T* p, float x, float y, float z, float w) {
+  if constexpr (std::is_same<T, float>::value) {
+    *reinterpret_cast<float4*>(p) = make_float4(x, y, z, w);
+  } else {
+    T v[4] = {Elem<T>::from_float(x), Elem<T>::from_float(y), Elem<T>::from_float(z), Elem<T>::from_float(w)};
+    *reinterpret_cast<uint2*>(p) = *reinterpret_cast<const uint2*>(v);
+  }
+}
 
 
 template <typename T>
@@ -52,23 +68,28 @@ __global__ void __launch_bounds__(kExchangeThreads) exchange_merge_kernel(const 
                   ((size_t)par * a.world + a.rank) * a.slot_floats;
     const float4* src4 = reinterpret_cast<const float4*>(a.po);
     float4* dst4 = reinterpret_cast<float4*>(slot);
+#pragma unroll 4
     for (int i = threadIdx.x; i < n_o / 4; i += blockDim.x) dst4[i] = __ldg(src4 + i);
     for (int i = threadIdx.x; i < nbh; i += blockDim.x) slot[n_o + i] = __ldg(a.plse + i);
   }
-  __threadfence_system();
+  // release: every thread's stores, the barrier, one system-scope fence, the flag
   __syncthreads();
-  if (threadIdx.x == 0) st_release_sys(reinterpret_cast<unsigned long long*>(a.peers[dst]) + a.rank, e);
+  if (threadIdx.x == 0) {
+    fence_acq_rel_sys();
+    st_relaxed_sys(reinterpret_cast<unsigned long long*>(a.peers[dst]) + a.rank, e);
+  }
 
-  // 2. wait until every rank has published epoch e here (bounded)
+  // 2. wait until every rank has published epoch e here (bounded), then acquire
   if (threadIdx.x < a.world) {
     const unsigned long long t0 = global_timer_ns();
-    for (uint32_t it = 1; ld_acquire_sys(flags + threadIdx.x) < e; ++it) {
+    for (uint32_t it = 1; ld_relaxed_sys(flags + threadIdx.x) < e; ++it) {
       if ((it & 63u) == 0u && global_timer_ns() - t0 > a.wait_budget_ns) {
         flag_device_error(a.err, AICAS_DEVERR_PEER_TIMEOUT);
         timed_out = 1;
         break;
       }
     }
+    fence_acq_rel_sys();
   }
   __syncthreads();
 
@@ -80,11 +101,17 @@ __global__ void __launch_bounds__(kExchangeThreads) exchange_merge_kernel(const 
   for (int u = threadIdx.x; u < (r1 - r0) * q4; u += blockDim.x) {
     const int bh = r0 + u / q4, c4 = u % q4;
     const int b = bh / a.heads, h = bh % a.heads;
+    // every rank's lse and columns read at once, from L2 (this SM's L1 may
+    // hold the slot from two calls ago)
     float lse[kMaxExchangeRanks];
+    float4 ov[kMaxExchangeRanks];
     float M = -INFINITY;
 #pragma unroll
     for (int r = 0; r < kMaxExchangeRanks; ++r) {
-      lse[r] = (r < a.world && !timed_out) ? __ldcv(slots + (size_t)r * a.slot_floats + n_o + bh) : -INFINITY;
+      const bool in = r < a.world && !timed_out;
+      const float* sr = slots + (size_t)r * a.slot_floats;
+      lse[r] = in ? __ldcg(sr + n_o + bh) : -INFINITY;
+      ov[r] = in ? __ldcg(reinterpret_cast<const float4*>(sr + (size_t)bh * a.hd) + c4) : make_float4(0.f, 0.f, 0.f, 0.f);
       M = fmaxf(M, lse[r]);
     }
     float L = 0.f;
@@ -92,22 +119,17 @@ __global__ void __launch_bounds__(kExchangeThreads) exchange_merge_kernel(const 
     if (M != -INFINITY) {
 #pragma unroll
       for (int r = 0; r < kMaxExchangeRanks; ++r) {
-        if (r >= a.world) break;
-        const float w = exp2f(lse[r] - M);
-        const float4 o = __ldcv(reinterpret_cast<const float4*>(slots + (size_t)r * a.slot_floats + (size_t)bh * a.hd) + c4);
+        const float w = exp2f(lse[r] - M);  // 0 for ranks past the world
         L += w;
-        O.x = fmaf(w, o.x, O.x);
-        O.y = fmaf(w, o.y, O.y);
-        O.z = fmaf(w, o.z, O.z);
-        O.w = fmaf(w, o.w, O.w);
+        O.x = fmaf(w, ov[r].x, O.x);
+        O.y = fmaf(w, ov[r].y, O.y);
+        O.z = fmaf(w, ov[r].z, O.z);
+        O.w = fmaf(w, ov[r].w, O.w);
       }
     }
     const float inv = L > 0.f ? 1.f / L : 0.f;
     T* orow = static_cast<T*>(a.out) + (int64_t)b * a.o_sb + (int64_t)h * a.o_sh + 4 * c4;
-    orow[0] = Elem<T>::from_float(O.x * inv);
-    orow[1] = Elem<T>::from_float(O.y * inv);
-    orow[2] = Elem<T>::from_float(O.z * inv);
-    orow[3] = Elem<T>::from_float(O.w * inv);
+    store4<T>(orow, O.x * inv, O.y * inv, O.z * inv, O.w * inv);
     if (a.lse != nullptr && c4 == 0) a.lse[bh] = L > 0.f ? M + log2f(L) : -INFINITY;
   }
 
