@@ -77,8 +77,9 @@ struct DecodeArgs {
 
 // Exchange buffer layout, shared by the exchange kernel and the fused decode:
 //   [0, 256)      uint64 flags[32]: flags[src] = last epoch rank src published here
-//   [256, 264)    uint64 epoch: calls completed by the owner
-//   [264, 268)    uint32 CTAs of the current exchange-kernel call that have finished
+//   [256, 320)    uint64 epoch[8]: calls completed by the owner, one word per
+//                 exchange-kernel CTA (the fused decode reads word 0 and
+//                 advances the first `world` words)
 //   [512, slots)  uint64 pair_flags[B * H][8]: [pair][src] = last epoch rank src
 //                 published that (request, KV head) pair's partial here (fused decode)
 //   [slots, ...)  fp32 slots[2][world][slot_floats]: each source rank's (out, lse)

@@ -256,7 +256,7 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kThreads, G <= 2 ? 2 : 1)
   unsigned long long xe = 0;
   int xpar = 0;
   if constexpr (XCHG) {
-    xe = *reinterpret_cast<volatile unsigned long long*>(static_cast<uint8_t*>(a.xpeers[a.xrank]) + 256) + 1;
+    xe = *reinterpret_cast<volatile unsigned long long*>(static_cast<uint8_t*>(a.xpeers[a.xrank]) + 256) + 1;  // word 0
     xpar = (int)(xe & 1);
   }
 
@@ -664,8 +664,10 @@ __global__ void __launch_bounds__(DecodeCfg<T, D, G>::kThreads, G <= 2 ? 2 : 1)
         a.ws_sched[1] = 0u;
         if constexpr (XCHG) {
           a.ws_sched[2] = 0u;
-          // this call is complete on this rank
-          *reinterpret_cast<volatile unsigned long long*>(static_cast<uint8_t*>(a.xpeers[a.xrank]) + 256) = xe;
+          // this call is complete on this rank: every epoch word (one per
+          // exchange-kernel CTA) moves, so either kernel can make the next call
+          for (int r = 0; r < a.xworld; ++r)
+            reinterpret_cast<volatile unsigned long long*>(static_cast<uint8_t*>(a.xpeers[a.xrank]) + 256)[r] = xe;
         }
         __threadfence();
       }

@@ -14,8 +14,8 @@
 // buffer have reached the epoch and merges its share of the (request, head)
 // rows exactly as the single-device merge does:
 // o = sum_r 2^(lse_r - M) o_r / sum_r 2^(lse_r - M).
-// The last CTA to finish advances the epoch, so every CTA of a call reads the
-// same epoch whatever order they start in.
+// Each CTA index has its own epoch word, advanced by that CTA at its end, so
+// every CTA of a call reads the same epoch whatever order they start in.
 //
 // Slot reuse is safe with two parities: a rank overwrites parity p again only
 // in call e + 2, after its call e + 1 has seen every peer's flag for e + 1,
@@ -53,8 +53,9 @@ __global__ void __launch_bounds__(kExchangeThreads) exchange_merge_kernel(const 
   grid_dependency_wait();
   uint8_t* own = static_cast<uint8_t*>(a.peers[a.rank]);
   unsigned long long* flags = reinterpret_cast<unsigned long long*>(own);
-  unsigned long long* epoch_word = reinterpret_cast<unsigned long long*>(own + 256);
-  unsigned int* done_word = reinterpret_cast<unsigned int*>(own + 264);
+  // this CTA's epoch word (one per CTA index: no CTA waits for another to
+  // finish reading before the epoch can move)
+  unsigned long long* epoch_word = reinterpret_cast<unsigned long long*>(own + 256) + blockIdx.x;
   const unsigned long long e = *reinterpret_cast<volatile unsigned long long*>(epoch_word) + 1;
   const int par = (int)(e & 1);
   const int nbh = a.batch * a.heads;
@@ -133,16 +134,9 @@ __global__ void __launch_bounds__(kExchangeThreads) exchange_merge_kernel(const 
     if (a.lse != nullptr && c4 == 0) a.lse[bh] = L > 0.f ? M + log2f(L) : -INFINITY;
   }
 
-  // 4. the last CTA of this call advances the epoch: this call is complete on this rank
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    if (atomicAdd(done_word, 1u) == gridDim.x - 1) {
-      *done_word = 0u;
-      *epoch_word = e;
-      __threadfence();
-    }
-  }
+  // 4. this CTA's epoch word advances: the next call's CTA of the same index
+  // reads it only after this grid has completed
+  if (threadIdx.x == 0) *epoch_word = e;
 }
 
 }  // namespace
