@@ -746,31 +746,29 @@ __global__ void __launch_bounds__(kThreads, RP == 16 ? 2 : 1) decode_linear_kern
       }
       epi_sync();
       if (s_last) {
-        // every thread loads shares into shared memory (the ring is idle now),
-        // then R threads add them in share order
+        // a fixed order, in parallel: kTpr consecutive lanes per row each add
+        // every kTpr-th share (eight loads in flight), then a butterfly over
+        // those lanes
         fence_acq_rel_gpu();
+        constexpr int kTpr = kEpiThreads / RP;  // 8 or 4 lanes of one warp per row
         const int count = a.cs > 1 ? a.grid : a.tiles;
-        float* buf = reinterpret_cast<float*>(smem_raw + (ring - smem_u32(smem_raw)));
-        const int total = count * a.R;
-        for (int base = tid; base < total; base += 8 * kEpiThreads) {
-          float v[8];
+        const int r = tid / kTpr, j = tid % kTpr;
+        float ss = 0.f;
+        if (r < a.R) {
+          for (int e0 = j; e0 < count; e0 += 8 * kTpr) {
+            float v[8];
 #pragma unroll
-          for (int m = 0; m < 8; ++m) {
-            const int idx = base + m * kEpiThreads;
-            if (idx < total) v[m] = __ldcg(a.ss_part + (idx / a.R) * RP + idx % a.R);
-          }
+            for (int m = 0; m < 8; ++m) {
+              const int e = e0 + m * kTpr;
+              v[m] = e < count ? __ldcg(a.ss_part + e * RP + r) : 0.f;
+            }
 #pragma unroll
-          for (int m = 0; m < 8; ++m) {
-            const int idx = base + m * kEpiThreads;
-            if (idx < total) buf[idx] = v[m];
+            for (int m = 0; m < 8; ++m) ss += v[m];
           }
         }
-        epi_sync();
-        if (tid < a.R) {
-          float ss = 0.f;
-          for (int e = 0; e < count; ++e) ss += buf[e * a.R + tid];
-          a.sumsq_out[tid] = ss;
-        }
+#pragma unroll
+        for (int o = kTpr / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (j == 0 && r < a.R) a.sumsq_out[r] = ss;
       }
     }
   }
