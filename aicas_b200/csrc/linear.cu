@@ -672,7 +672,8 @@ __global__ void __launch_bounds__(kThreads, RP == 16 ? 2 : 1) decode_linear_kern
 #pragma unroll
           for (int r = 0; r < RP; ++r)
             if (r < a.R) mine[(p * RP + r) * kTileN + tid] = acc[p][r];
-        fence_acq_rel_gpu();
+        // the barrier orders every thread's stores before thread 0's release
+        // (cumulative): one fence for the CTA, in the atomic
         epi_sync();
         if (tid == 0) {
           const unsigned int old = atom_add_acq_rel(a.counters + t, 1u);
@@ -735,8 +736,8 @@ __global__ void __launch_bounds__(kThreads, RP == 16 ? 2 : 1) decode_linear_kern
       }
     }
     if (a.sumsq_out != nullptr && !aborted) {
-      // the last CTA to finish adds the shares up in a fixed order
-      fence_acq_rel_gpu();
+      // the last CTA to finish adds the shares up in a fixed order (the
+      // barrier orders the shares' stores before thread 0's release)
       epi_sync();
       if (tid == 0) {
         const unsigned int old = atom_add_acq_rel(a.counters + kDoneSlot, 1u);
