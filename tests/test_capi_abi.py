@@ -218,6 +218,14 @@ def test_exchange_buffer_size_and_validation(native_lib):
     p.head_dim = 130
     assert native_lib.aicas_exchange_merge(ctypes.byref(p), None) == nat.ERR_INVALID
     assert "multiple of 4" in nat.last_error()
+    # the merge writes four outputs a store: out aligned, strides multiples of 16 bytes
+    p.head_dim = 128
+    p.out = (3 << 20) + 8
+    assert native_lib.aicas_exchange_merge(ctypes.byref(p), None) == nat.ERR_INVALID
+    assert "16-byte aligned" in nat.last_error()
+    p.out, p.o_stride_b, p.o_stride_h = 3 << 20, 16 * 128, 132
+    assert native_lib.aicas_exchange_merge(ctypes.byref(p), None) == nat.ERR_INVALID
+    assert "multiples of 16 bytes" in nat.last_error()
     assert native_lib.aicas_peer_buffer_alloc(0, None, None) == nat.ERR_INVALID
     assert native_lib.aicas_peer_buffer_open(None, None) == nat.ERR_INVALID
 
