@@ -267,7 +267,39 @@ __global__ void __launch_bounds__(threads_for<KT>(), 3 - KT) fmha_fwd_kernel(con
       const int H = a.hq;
       int target = blockIdx.x / H;
       int found = -1, pr = 0, qs = 0, ql = 0, ks = 0, kl = 0;
-      for (int base = 0; base < a.num_seqs && found < 0; base += 32) {
+      if (a.num_seqs <= 32) {
+        // up to 32 sequences (a batch of images): the longest keys first, so
+        // that the CTAs handed out last are short ones and the launch ends
+        // together (ties by index); a row block's work grows with the key
+        // length, and CTAs are handed out in blockIdx order
+        const int i = lane;
+        int np = 0, qsi = 0, qei = 0, ksi = 0, kei = 0, klen = -1;
+        if (i < a.num_seqs) {
+          qsi = min(max(a.cu_q[i], 0), a.seq_q);
+          qei = min(max(a.cu_q[i + 1], qsi), a.seq_q);
+          ksi = min(max(a.cu_k[i], 0), a.seq_kv);
+          kei = min(max(a.cu_k[i + 1], ksi), a.seq_kv);
+          np = (qei - qsi + KT * kBM - 1) / (KT * kBM);
+          klen = kei - ksi;
+        }
+        int excl = 0;  // row blocks of the sequences ordered before this one
+        for (int j = 0; j < 32; ++j) {
+          const int kj = __shfl_sync(0xffffffffu, klen, j);
+          const int npj = __shfl_sync(0xffffffffu, np, j);
+          if (kj > klen || (kj == klen && j < i)) excl += npj;
+        }
+        const unsigned ball = __ballot_sync(0xffffffffu, i < a.num_seqs && target >= excl && target < excl + np);
+        if (ball) {
+          const int src = __ffs(ball) - 1;
+          found = src;
+          pr = target - __shfl_sync(0xffffffffu, excl, src);
+          qs = __shfl_sync(0xffffffffu, qsi, src);
+          ql = __shfl_sync(0xffffffffu, qei - qsi, src);
+          ks = __shfl_sync(0xffffffffu, ksi, src);
+          kl = __shfl_sync(0xffffffffu, kei - ksi, src);
+        }
+      }
+      for (int base = 0; a.num_seqs > 32 && base < a.num_seqs && found < 0; base += 32) {
         const int i = base + lane;
         int np = 0, qsi = 0, qei = 0, ksi = 0, kei = 0;
         if (i < a.num_seqs) {
